@@ -1,0 +1,478 @@
+#!/usr/bin/env python
+"""Benchmark of the constrained beam step (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl ours|reference]
+
+A "step" is one beam-search step of every request of the configured batch:
+logits rows [R*B, V] -> new beams.  Steps cycle through the catalog levels
+(root, level 1, level 2, ...) carrying the beams forward, as in a real
+3-token semantic-ID decode, and restart at the root after the last level.
+
+metric: constrained beam-steps/s = requests x steps / time (whole job), plus
+the achieved HBM bandwidth of the fused kernel against the measured copy
+bandwidth in MEASURED_PEAKS.json.  Logits are synthetic N(0, sigma^2) from a
+seeded torch.Generator, each step's logits (>= 1.2 GB) exceed the 126 MB L2,
+so no flush is needed between iterations.
+
+--gpus N (under torchrun): requests are sharded, every rank runs its own
+batch of the configured size (weak scaling, no collective on the data path);
+the time is the max over ranks of the device-timed region.
+--impl reference: the CPU restatement of the reference's step (the oracle
+port) on the host cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from vllm_gr_ehaleva_b200.synthetic import CONFIGS, histories, initial_cum, make_catalog  # noqa: E402
+
+METRIC = "constrained beam-steps/sec (requests x steps)"
+UNIT = "req-steps/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="cfg2", choices=["cfg2", "cfg3", "cfg4"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--requests", type=int, default=None, help="override requests per GPU")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append([x.strip() for x in line.split(",")])
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            try:
+                sm.append(float(s[1]))
+                mx = float(s[2])
+                for n, v in zip(names, s[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+            except Exception:
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ workload
+def build_workload(cfg_name: str, requests: int | None, device):
+    import torch
+    from vllm_gr_ehaleva_b200.synthetic import logits_torch
+    cfg = dict(CONFIGS[cfg_name])
+    R = requests or cfg["requests"]
+    B, V = cfg["beams"], cfg["vocab"]
+    dtype = {"bf16": torch.bfloat16, "f32": torch.float32}[cfg["dtype"]]
+    wl = {"cfg": cfg, "R": R, "B": B, "V": V, "dtype": dtype}
+    if cfg["levels"]:
+        cat = make_catalog(cfg["items"], cfg["levels"], cfg["codebook"], V, cfg["zipf"], seed=1)
+        wl["catalog"] = cat
+        wl["levels"] = cfg["levels"]
+        wl["csr_dev"] = (torch.from_numpy(cat.csr.row_ptr).to(device), torch.from_numpy(cat.csr.child_tok).to(device),
+                         torch.from_numpy(cat.csr.child_node).to(device))
+    else:
+        wl["catalog"] = None
+        wl["levels"] = 2        # unconstrained: alternate two logits buffers
+        wl["csr_dev"] = None
+    nbuf = wl["levels"]
+    wl["logits"] = [logits_torch(R * B, V, cfg["sigma"], seed=100 + i, dtype=dtype, device=device) for i in range(nbuf)]
+    return wl
+
+
+def initial_state(wl, device):
+    import torch
+    R, B = wl["R"], wl["B"]
+    cum = torch.from_numpy(initial_cum(R, B)).to(device)
+    if wl["catalog"] is not None:
+        node = torch.full((R, B), wl["catalog"].start_node, dtype=torch.int32, device=device)
+        hist = torch.full((R, B, 1), wl["catalog"].sid_begin, dtype=torch.int32, device=device)
+    else:
+        node = torch.full((R, B), -1, dtype=torch.int32, device=device)
+        hist = torch.from_numpy(histories(R, B, wl["cfg"]["hist"], wl["V"], seed=3)).to(device)
+    return cum, node, hist
+
+
+def step_kwargs(wl):
+    cfg = wl["cfg"]
+    kw = dict(beam_width=wl["B"], csr=wl["csr_dev"], vocab_size=wl["V"])
+    if cfg["mode"] == "processed":
+        R = wl["R"]
+        kw.update(logprobs_mode="processed_logprobs", temperature=[cfg["temperature"]] * R,
+                  repetition_penalty=[cfg["rep"]] * R, presence_penalty=[cfg["pres"]] * R,
+                  frequency_penalty=[cfg["freq"]] * R, eos_token_id=None)
+    return kw
+
+
+def algorithmic_bytes(wl, node_np: np.ndarray, hist_len: int) -> int:
+    """Bytes the step must move for R requests ('algorithmic bytes')."""
+    R, B, V = wl["R"], wl["B"], wl["V"]
+    s = 2 if wl["cfg"]["dtype"] == "bf16" else 4
+    total = R * B * V * s                       # every logit read once
+    total += R * B * 12                         # cum, node, lse
+    total += R * (2 * B * 12 + B * 16)          # candidates + selected beams
+    total += R * (B * hist_len * 4 + B * (hist_len + 1) * 4)   # fork table read + write
+    if wl["catalog"] is not None:
+        deg = wl["catalog"].csr.degree
+        for r in range(R):
+            nodes = np.unique(node_np[r][node_np[r] >= 0])
+            total += int(np.sum(8 + 8 * deg(nodes)))
+    else:
+        total += R * B * hist_len * 4           # penalty histories (same buffer as the fork table)
+    return int(total)
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from vllm_gr_ehaleva_b200.sample import beam_step
+    from vllm_gr_ehaleva_b200.sample.beam_search_sampler import Workspace
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    device = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(device)
+    wl = build_workload(args.config, args.requests, device)
+    R, B = wl["R"], wl["B"]
+    kw = step_kwargs(wl)
+    ws = Workspace(device)
+    levels = wl["levels"]
+    cum0, node0, hist0 = initial_state(wl, device)
+    stream = torch.cuda.current_stream(device)
+
+    # state per level so that each timed step sees the catalog level it would in a decode
+    def run_chain(n_steps, record=None, bytes_acc=None):
+        cum, node, hist = cum0, node0, hist0
+        lvl = 0
+        for i in range(n_steps):
+            if bytes_acc is not None:
+                bytes_acc.append(algorithmic_bytes(wl, node.cpu().numpy(), hist.shape[2]))
+            if record is not None:
+                record[i][0].record(stream)
+            out = beam_step(wl["logits"][lvl], cum, node, hist=hist, workspace=ws, **kw)
+            if record is not None:
+                record[i][1].record(stream)
+            lvl += 1
+            if lvl == levels:
+                lvl = 0
+                cum, node, hist = cum0, node0, hist0
+            else:
+                cum, node, hist = out.sel_score, out.sel_node, out.hist_out
+                if wl["catalog"] is None:
+                    hist = hist0      # unconstrained: keep the fixed-length penalty history
+        return out
+
+    # algorithmic bytes of one cycle of levels (host-side, outside timing)
+    bytes_cycle = []
+    run_chain(levels, bytes_acc=bytes_cycle)
+    out = run_chain(max(args.warmup, 3))
+    torch.cuda.synchronize()
+    err = int(out.err.item())
+
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    clocks = ClockSampler(device.index if world == 1 else local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    out = run_chain(args.steps, record=events)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    elapsed_ms = t0.elapsed_time(t1)
+    per_step_ms = [a.elapsed_time(b) for a, b in events]
+    err |= int(out.err.item())
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+
+    # roofline of the fused kernel: algorithmic bytes / device time of each step
+    steps_bytes = [bytes_cycle[i % levels] for i in range(args.steps)]
+    avg_launch_ms = float(np.mean(per_step_ms))
+    achieved = float(np.mean([b / (ms * 1e-3) for b, ms in zip(steps_bytes, per_step_ms)])) / 1e9
+    peak, peak_kind = peaks()
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, wl, kw, ws, device, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(wl, budget_s=15.0)
+
+    value = world * R * args.steps / (elapsed_ms * 1e-3)
+    res = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(elapsed_ms / args.steps, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": wl["cfg"]["dtype"], "data": "synthetic (seeded N(0, sigma^2) logits, Zipf catalog)",
+        "config": {"workload": args.config, "requests_per_gpu": R, "beam_width": B, "vocab": wl["V"],
+                   "catalog_items": None if wl["catalog"] is None else wl["catalog"].num_items,
+                   "levels": wl["cfg"]["levels"], "logprobs_mode": wl["cfg"]["mode"],
+                   "parallelism": f"request-sharded x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (>= 1.2 GB logits per step), no flush"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": None, "kernel": "gr::fused_step_kernel",
+                     "algorithmic_bytes_per_launch": int(np.mean(steps_bytes)),
+                     "avg_launch_ms": round(avg_launch_ms, 5)},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+        "device_errors": err,
+    }
+    if e2e is not None:
+        res["e2e"] = e2e
+    if cpu is not None:
+        res["cpu_baseline"] = cpu
+    prof = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(prof):
+        try:
+            with open(prof) as f:
+                tr = json.load(f).get(args.config)
+            if tr:
+                res["roofline"]["traffic"] = tr
+        except Exception:
+            pass
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(args, wl, kw, ws, device, world):
+    """Same metric through the public API with host (pinned) input and output buffers:
+    every step copies its logits host->device and reads the new beams back."""
+    import torch
+    from vllm_gr_ehaleva_b200.sample import beam_step
+    R, B = wl["R"], wl["B"]
+    host_logits = [x.cpu().pin_memory() for x in wl["logits"]]
+    dev_buf = torch.empty_like(wl["logits"][0])
+    cum0, node0, hist0 = initial_state(wl, device)
+    levels = wl["levels"]
+    stream = torch.cuda.current_stream(device)
+    host_out = {k: torch.empty((R, B), dtype=dt).pin_memory()
+                for k, dt in (("sel_score", torch.float32), ("sel_token", torch.int32), ("sel_parent", torch.int32))}
+    steps = max(3, min(args.steps, 10))
+
+    def one(i, cum, node, hist):
+        lvl = i % levels
+        dev_buf.copy_(host_logits[lvl], non_blocking=True)
+        out = beam_step(dev_buf, cum, node, hist=hist, workspace=ws, **kw)
+        for k in host_out:
+            host_out[k].copy_(getattr(out, k), non_blocking=True)
+        return out
+
+    def chain(n):
+        cum, node, hist = cum0, node0, hist0
+        for i in range(n):
+            out = one(i, cum, node, hist)
+            if (i + 1) % levels == 0:
+                cum, node, hist = cum0, node0, hist0
+            else:
+                cum, node, hist = out.sel_score, out.sel_node, (out.hist_out if wl["catalog"] is not None else hist0)
+        return out
+
+    chain(levels)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    chain(steps)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    h2d = wl["logits"][0].numel() * wl["logits"][0].element_size()
+    d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+    return {"value": round(world * R * steps / (ms * 1e-3), 2), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "steps": steps}
+
+
+# ------------------------------------------------------------------ CPU arms
+def cpu_sample_inputs(wl_cfg, n_requests: int, seed: int = 0):
+    """Host copy of one root-level step of `n_requests` requests (the costliest level)."""
+    from oracle.restated import bf16_bits_to_f32, f32_to_bf16_bits
+    cfg = wl_cfg
+    B, V = cfg["beams"], cfg["vocab"]
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((n_requests, B, V), dtype=np.float32) * np.float32(cfg["sigma"]))
+    if cfg["dtype"] == "bf16":
+        x = bf16_bits_to_f32(f32_to_bf16_bits(x))
+    return x
+
+
+def cpu_step_time(cfg, cat, n_req: int, threads: int, budget_s: float):
+    """Time the oracle port on n_req requests of one root-level step, rows spread
+    over `threads` host threads.  Returns (seconds, requests done)."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import restated as O
+    B, V = cfg["beams"], cfg["vocab"]
+    x = cpu_sample_inputs(cfg, n_req)
+    cum = initial_cum(n_req, B)
+    if cat is not None:
+        node = np.full((n_req, B), cat.start_node, np.int32)
+        csr = O.CSR(cat.csr.row_ptr, cat.csr.child_tok, cat.csr.child_node)
+        hist = np.full((n_req, B, 1), cat.sid_begin, np.int32)
+        kw = {}
+    else:
+        node = np.full((n_req, B), -1, np.int32)
+        csr = None
+        hist = histories(n_req, B, cfg["hist"], V, seed=3)
+        kw = dict(logprobs_mode=O.PROCESSED, temperature=[cfg["temperature"]] * n_req,
+                  rep_penalty=[cfg["rep"]] * n_req, pres_penalty=[cfg["pres"]] * n_req,
+                  freq_penalty=[cfg["freq"]] * n_req)
+
+    def one(r):
+        return O.beam_step(x[r:r + 1], cum[r:r + 1], node[r:r + 1], csr, beam_width=B, vocab_size=V,
+                           hist_in=hist[r:r + 1], **{k: (v[r:r + 1] if isinstance(v, list) else v) for k, v in kw.items()})
+
+    t0 = time.perf_counter()
+    done = 0
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        futs = [ex.submit(one, r) for r in range(n_req)]
+        for f in futs:
+            f.result()
+            done += 1
+    return time.perf_counter() - t0, done
+
+
+def cpu_baseline(wl, budget_s=15.0):
+    cfg = wl["cfg"]
+    threads = len(os.sched_getaffinity(0))
+    n_req = max(1, min(wl["R"], threads))
+    secs, done = cpu_step_time(cfg, wl["catalog"], n_req, threads, budget_s)
+    return {"value": round(done / secs, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{done} requests x 1 root-level step of {wl['cfg']['beams']} beams (oracle/restated.py, "
+                      f"one request per thread)", "cpu_model": cpu_model()}
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    """Reference arm: the oracle port of the reference's CPU step, all host threads."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = dict(CONFIGS[args.config])
+    cat = None
+    if cfg["levels"]:
+        cat = make_catalog(cfg["items"], cfg["levels"], cfg["codebook"], cfg["vocab"], cfg["zipf"], seed=1)
+    threads = len(os.sched_getaffinity(0))
+    n_req = max(1, threads)
+    for _ in range(max(args.warmup, 0) and 1):
+        cpu_step_time(cfg, cat, 1, 1, 5.0)
+    tot_s, tot_r = 0.0, 0
+    steps = max(1, min(args.steps, 3))
+    for _ in range(steps):
+        s, d = cpu_step_time(cfg, cat, n_req, threads, 30.0)
+        tot_s += s
+        tot_r += d
+    value = tot_r / tot_s
+    res = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": 0,
+           "steps": steps, "warmup": 1, "ms_per_step": round(1e3 * tot_s / steps, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
+           "config": {"workload": args.config, "beam_width": cfg["beams"], "vocab": cfg["vocab"]},
+           "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                            "sample": f"{n_req} requests x 1 root-level step per timed step",
+                            "cpu_model": cpu_model()},
+           "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(res), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,196 @@
+/*
+ * gr_beam.h — C ABI of the B200-native constrained beam-search step.
+ *
+ * One call of gr_beam_step() advances R beam-search requests by one decode
+ * step.  For every request it
+ *   1. takes each beam's next-token logits row (bf16 / f16 / f32),
+ *   2. normalises it over the whole vocabulary in vLLM's log-prob domain
+ *      (raw: log_softmax(x); processed: log_softmax(penalise(x) / T)),
+ *   3. restricts each beam to its candidate tokens: the children of its node
+ *      in the item-catalog trie (CSR), or all tokens for an unconstrained beam,
+ *      or (reference-literal mode) the beam's own top-K tokens with the
+ *      disallowed ones set to -inf,
+ *   4. adds the beam's cumulative score, moves EOS candidates out of the pool,
+ *   5. selects the top 2*beam_width (token, parent) candidates of the request
+ *      in canonical order: score descending, then flat index parent*V+token
+ *      ascending,
+ *   6. emits the first beam_width of them as the new beams together with the
+ *      child trie node and the forked per-beam token table.
+ *
+ * It replaces, as one device call, the per-step work of the reference
+ * (vLLM-GR) that is spread over:
+ *   - vLLM Sampler.forward -> compute_logprobs / gather_logprobs
+ *     (vllm v1/sample/sampler.py:67-140, 300-352; penalties :366-433),
+ *   - vllm_gr/logprobs.py:34-53           extract_and_dedup_flat_logprobs,
+ *   - vllm_gr/entrypoints/openai/serving_models.py:42-49  Catalog.valid,
+ *   - vllm_gr/entrypoints/openai/serving_engine.py:457-597 (mask, cum add,
+ *     EOS -> completed, argpartition top-B, new beams, fork_info),
+ *   - vllm_gr/entrypoints/llm.py:201-280   (same selection, offline),
+ *   - vllm_gr/csrc/minheap.cpp:75-114      (striped bounded top-N).
+ *
+ * Conventions
+ *   - Every pointer is a device pointer unless stated otherwise.  The caller
+ *     owns (allocates and frees) every buffer, including the workspace; the
+ *     library allocates no device memory.
+ *   - Calls are stream ordered and never synchronise the host.  `stream` is a
+ *     cudaStream_t passed as void* (NULL = the legacy default stream).
+ *   - Return value 0 = success, negative = gr_status error.  No call aborts,
+ *     throws or traps.  Errors found on the device (bad node id, CSR child
+ *     token out of range, a bounded wait that ran out) are OR-ed into the
+ *     caller's device error word io->err as GR_DEVERR_* bits.
+ *   - The workspace must be at least gr_beam_step_workspace_size() bytes and
+ *     256-byte aligned.  Its contents need not be initialised.
+ *   - Calls that share a workspace must not overlap on the GPU.
+ */
+#ifndef GR_BEAM_H_
+#define GR_BEAM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GR_ABI_VERSION 1
+
+typedef enum gr_status {
+  GR_OK = 0,
+  GR_ERR_NULL = -1,          /* a required pointer is NULL                    */
+  GR_ERR_BAD_DESC = -2,      /* sizes / ids out of range or inconsistent      */
+  GR_ERR_DTYPE = -3,         /* unsupported logit dtype or logprobs mode      */
+  GR_ERR_MISALIGNED = -4,    /* workspace not 256-byte aligned                */
+  GR_ERR_WORKSPACE = -5,     /* workspace smaller than required               */
+  GR_ERR_UNSUPPORTED = -6,   /* valid request outside this build's limits     */
+  GR_ERR_CUDA = -7,          /* a CUDA runtime call or launch failed          */
+  GR_ERR_NO_DEVICE = -8      /* no sm_100 device is current                   */
+} gr_status;
+
+/* Bits OR-ed into *io->err by the kernels. */
+#define GR_DEVERR_BAD_NODE      0x1   /* node id outside [-2, num_nodes)        */
+#define GR_DEVERR_BAD_CHILD     0x2   /* CSR child token outside [0, vocab)     */
+#define GR_DEVERR_TIMEOUT       0x4   /* a bounded mbarrier wait ran out        */
+#define GR_DEVERR_OVERFLOW      0x8   /* per-request candidate buffer overflow  */
+#define GR_DEVERR_TIE_BOUNDARY  0x10  /* streamed top-k boundary not exact      */
+
+typedef enum gr_dtype {
+  GR_DTYPE_F32 = 0,
+  GR_DTYPE_BF16 = 1,
+  GR_DTYPE_F16 = 2
+} gr_dtype;
+
+/* vLLM LogprobsMode (vllm config/model.py): "raw_logprobs" is log_softmax of
+ * the raw logits, "processed_logprobs" is log_softmax after penalties and
+ * temperature (vllm v1/sample/sampler.py:80-88, 223-233, 262-265). */
+typedef enum gr_logprobs_mode {
+  GR_LOGPROBS_RAW = 0,
+  GR_LOGPROBS_PROCESSED = 1
+} gr_logprobs_mode;
+
+/* Node id conventions for io->node / sel_node. */
+#define GR_NODE_UNCONSTRAINED (-1)  /* every vocab token is a candidate       */
+#define GR_NODE_DEAD (-2)           /* prefix not in the catalog: no children */
+
+typedef struct gr_step_desc {
+  int32_t num_requests;   /* R                                                */
+  int32_t num_beams;      /* beam rows per request in this step (>= 1)        */
+  int32_t beam_width;     /* B: beams kept; 2*B candidates are emitted        */
+  int32_t vocab_size;     /* V: full vocabulary (token ids are in [0, V))     */
+  int32_t vocab_local;    /* columns present in `logits` (== V unsharded)     */
+  int32_t vocab_offset;   /* token id of column 0 (0 unsharded)               */
+  int64_t row_stride;     /* elements between consecutive logit rows          */
+  int32_t logit_dtype;    /* gr_dtype                                         */
+  int32_t logprobs_mode;  /* gr_logprobs_mode                                 */
+  int32_t per_beam_k;     /* 0: all allowed children are candidates;
+                             K>0: reference-literal, each beam's raw top-K
+                             (after the sampled-token dedup) then masked      */
+  int32_t eos_token_id;   /* -1: no EOS handling (ignore_eos)                 */
+  int32_t hist_len;       /* T: tokens per beam in hist_in (fork table and,
+                             in processed mode, the penalty history)          */
+  int32_t num_nodes;      /* N: CSR trie nodes (0 if no catalog)              */
+  int64_t num_edges;      /* E: CSR trie edges                                */
+} gr_step_desc;
+
+typedef struct gr_step_io {
+  /* inputs */
+  const void* logits;          /* [R*num_beams rows][row_stride], dtype desc  */
+  const float* cum;            /* [R*num_beams] cumulative beam scores        */
+  const int32_t* node;         /* [R*num_beams] trie node of each beam        */
+  const int64_t* row_ptr;      /* [N+1] CSR offsets (may be NULL if N == 0)   */
+  const int32_t* child_tok;    /* [E] child token ids, ascending per node     */
+  const int32_t* child_node;   /* [E] child node ids                          */
+  const float* temperature;    /* [R] or NULL (= 1); T < 1e-5 means 1         */
+  const float* rep_penalty;    /* [R] or NULL (= 1)                           */
+  const float* pres_penalty;   /* [R] or NULL (= 0)                           */
+  const float* freq_penalty;   /* [R] or NULL (= 0)                           */
+  const int32_t* hist_in;      /* [R*num_beams][T] generated tokens, or NULL
+                                  when T == 0; entries < 0 are padding        */
+  /* outputs (all required unless marked optional) */
+  float* cand_score;           /* [R][2B] sorted canonical candidates         */
+  int32_t* cand_token;         /* [R][2B]  (-1 padding)                       */
+  int32_t* cand_parent;        /* [R][2B]  (-1 padding)                       */
+  float* sel_score;            /* [R][B] new cumulative scores                */
+  int32_t* sel_token;          /* [R][B]                                      */
+  int32_t* sel_parent;         /* [R][B] parent beam index within request     */
+  int32_t* sel_node;           /* [R][B] child trie node (-1/-2 as above)     */
+  float* eos_score;            /* [R*num_beams] cum+lp of the beam's EOS
+                                  candidate, NaN if it had none (optional)    */
+  int32_t* hist_out;           /* [R][B][T+1] forked token table (optional)   */
+  float* lse;                  /* [R*num_beams] row log-sum-exp (optional)    */
+  int32_t* err;                /* device error word, GR_DEVERR_* bits         */
+} gr_step_io;
+
+/* Library ABI version (GR_ABI_VERSION). */
+int32_t gr_abi_version(void);
+
+/* Human-readable name of a gr_status value (static string). */
+const char* gr_status_string(int32_t status);
+
+/* Bytes of workspace gr_beam_step() needs for `desc`.
+ * Replaces nothing in the reference (the reference allocates per step in
+ * Python lists / NumPy arrays: serving_engine.py:457-535). */
+int32_t gr_beam_step_workspace_size(const gr_step_desc* desc, size_t* bytes);
+
+/* One constrained beam-search step for all requests (see top of file).
+ * Replaces: vllm v1/sample/sampler.py:67-140 (logprobs) +
+ * vllm_gr/logprobs.py:34-53 + serving_engine.py:457-597 / llm.py:201-280. */
+int32_t gr_beam_step(const gr_step_desc* desc, const gr_step_io* io,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- vocab-sharded lm_head (logit columns split over ranks) --------------
+ *
+ * Phase 1 (every shard): per-row partial (max, sum exp(x - max)) over the
+ * local columns, written as float2 pairs to partials[row] = {max, sumexp}.
+ * Replaces the full-row log_softmax of vllm sampler.py:300-301 after the
+ * tensor-parallel logits all-gather (vllm logits_processor.py:75-86).
+ */
+int32_t gr_lse_partials(const gr_step_desc* desc, const void* logits,
+                        const float* temperature, const float* rep_penalty,
+                        const float* pres_penalty, const float* freq_penalty,
+                        const int32_t* hist_in, float* partials,
+                        int32_t* err, void* stream);
+
+/* Phase 2 (every shard, after the caller all-gathered the partials of all
+ * `num_shards` shards into gathered_partials[num_shards][R*num_beams][2]):
+ * combines them into the global row lse, forms this shard's candidates and
+ * writes the shard's canonical top-2B per request to
+ * shard_keys[R][2B] (uint64 keys, see gr_key_decode in the Python layer).
+ * Constrained (per_beam_k == 0) mode only. */
+int32_t gr_shard_candidates(const gr_step_desc* desc, const gr_step_io* io,
+                            const float* gathered_partials, int32_t num_shards,
+                            uint64_t* shard_keys, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* Phase 3 (every shard, after the caller all-gathered shard_keys of all
+ * shards into gathered_keys[num_shards][R][2B]): merges them into the global
+ * top-2B per request and writes cand_* / sel_* / hist_out of `io` (the logits
+ * field is unused).  Every shard computes the same result. */
+int32_t gr_merge_candidates(const gr_step_desc* desc, const gr_step_io* io,
+                            const uint64_t* gathered_keys, int32_t num_shards,
+                            void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GR_BEAM_H_ */

@@ -1,0 +1,197 @@
+"""Shared test helpers: seeded step cases and GPU-vs-oracle comparison."""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from oracle import restated as O
+from vllm_gr_ehaleva_b200.catalog import csr_from_sequences
+from vllm_gr_ehaleva_b200.synthetic import make_catalog
+
+OUT_KEYS = ("cand_score", "cand_token", "cand_parent", "sel_score", "sel_token", "sel_parent",
+            "sel_node", "eos_score", "hist_out", "lse")
+
+
+@dataclass
+class Case:
+    logits32: np.ndarray            # [R, NB, VL] float32 (already rounded to the storage dtype)
+    dtype: str                      # "f32" | "bf16" | "f16"
+    cum: np.ndarray                 # [R, NB] float32
+    node: np.ndarray                # [R, NB] int32
+    beam_width: int
+    vocab_size: int
+    vocab_offset: int = 0
+    csr: object = None              # CSRTrie or None
+    hist: np.ndarray | None = None  # [R, NB, T] int32
+    mode: str = "raw_logprobs"
+    per_beam_k: int = 0
+    eos: int = -1
+    temperature: list | None = None
+    rep: list | None = None
+    pres: list | None = None
+    freq: list | None = None
+    row_pad: int = 0                # extra elements per row (unaligned stride)
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def R(self):
+        return self.cum.shape[0]
+
+    @property
+    def NB(self):
+        return self.cum.shape[1]
+
+
+def round_to(x32: np.ndarray, dtype: str) -> np.ndarray:
+    if dtype == "f32":
+        return x32.astype(np.float32)
+    if dtype == "bf16":
+        return O.bf16_bits_to_f32(O.f32_to_bf16_bits(x32))
+    if dtype == "f16":
+        return x32.astype(np.float16).astype(np.float32)
+    raise ValueError(dtype)
+
+
+def small_catalog(V=8192, L=3, C=512, items=20000, zipf=1.1, seed=1):
+    return make_catalog(items, L, C, V, zipf, seed=seed)
+
+
+def make_logits(R, NB, VL, sigma, seed, dtype):
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((R, NB, VL), dtype=np.float32) * np.float32(sigma)).astype(np.float32)
+    return round_to(x, dtype)
+
+
+def oracle_step(case: Case, arith="reference", lse_override=None) -> dict:
+    return O.beam_step(
+        case.logits32, case.cum, case.node,
+        None if case.csr is None else O.CSR(case.csr.row_ptr, case.csr.child_tok, case.csr.child_node),
+        beam_width=case.beam_width, vocab_size=case.vocab_size, vocab_offset=case.vocab_offset,
+        logprobs_mode=O.PROCESSED if case.mode == "processed_logprobs" else O.RAW,
+        per_beam_k=case.per_beam_k, eos_token_id=case.eos, hist_in=case.hist,
+        temperature=case.temperature, rep_penalty=case.rep, pres_penalty=case.pres,
+        freq_penalty=case.freq, arith=arith, lse_override=lse_override)
+
+
+# --------------------------------------------------------------------------- GPU side
+def to_device_logits(case: Case, device):
+    import torch
+    R, NB, VL = case.logits32.shape
+    if case.dtype == "f32":
+        t = torch.from_numpy(case.logits32.copy())
+    elif case.dtype == "bf16":
+        bits = O.f32_to_bf16_bits(case.logits32).astype(np.int16)
+        t = torch.from_numpy(bits).view(torch.bfloat16)
+    else:
+        t = torch.from_numpy(case.logits32.astype(np.float16))
+    t = t.reshape(R * NB, VL)
+    if case.row_pad:
+        buf = torch.zeros((R * NB, VL + case.row_pad), dtype=t.dtype)
+        buf[:, :VL] = t
+        t = buf.to(device)[:, :VL]
+        return t
+    return t.to(device)
+
+
+def gpu_step(case: Case, device="cuda", sampler_kwargs=None):
+    import torch
+    from vllm_gr_ehaleva_b200.sample import beam_step
+    logits = to_device_logits(case, device)
+    csr = None
+    if case.csr is not None:
+        csr = (torch.from_numpy(case.csr.row_ptr).to(device), torch.from_numpy(case.csr.child_tok).to(device),
+               torch.from_numpy(case.csr.child_node).to(device))
+    hist = None if case.hist is None else torch.from_numpy(case.hist).to(device)
+    out = beam_step(logits, torch.from_numpy(case.cum).to(device), torch.from_numpy(case.node).to(device),
+                    beam_width=case.beam_width, csr=csr, vocab_size=case.vocab_size,
+                    vocab_offset=case.vocab_offset, logprobs_mode=case.mode, per_beam_k=case.per_beam_k,
+                    eos_token_id=None if case.eos < 0 else case.eos, hist=hist,
+                    temperature=case.temperature, repetition_penalty=case.rep, presence_penalty=case.pres,
+                    frequency_penalty=case.freq, **(sampler_kwargs or {}))
+    torch.cuda.synchronize()
+    res = {k: getattr(out, k).cpu().numpy() for k in OUT_KEYS}
+    res["err"] = int(out.err.item())
+    return res
+
+
+# --------------------------------------------------------------------------- comparison
+def assert_bit_exact(gpu: dict, ref: dict, keys=OUT_KEYS):
+    """Every output identical (floats compared bit for bit, NaN == NaN)."""
+    for k in keys:
+        a, b = np.asarray(gpu[k]), np.asarray(ref[k])
+        assert a.shape == b.shape, f"{k}: shape {a.shape} vs {b.shape}"
+        if a.dtype.kind == "f":
+            same = (a.view(np.uint32) == b.astype(np.float32).view(np.uint32)) | (np.isnan(a) & np.isnan(b))
+            if not same.all():
+                idx = np.argwhere(~same)[:5]
+                raise AssertionError(f"{k} differs at {idx.tolist()}: gpu {a[~same][:5]} ref {b[~same][:5]}")
+        else:
+            if not np.array_equal(a, b):
+                idx = np.argwhere(a != b)[:5]
+                raise AssertionError(f"{k} differs at {idx.tolist()}: gpu {a[a != b][:5]} ref {b[a != b][:5]}")
+
+
+def assert_close_selection(gpu: dict, ref: dict, rel_tol: float, case: Case | None = None):
+    """Reference-arithmetic comparison.  Candidate (parent, token) sets must agree
+    except for entries whose score is within rel_tol of the request's boundary
+    score (near-ties that a last-ulp difference in lse can reorder).  Scores of
+    matching entries agree within rel_tol; the GPU list is canonically sorted."""
+    R, K2 = ref["cand_token"].shape
+    near_ties = 0
+    for r in range(R):
+        gs, gt, gp = gpu["cand_score"][r], gpu["cand_token"][r], gpu["cand_parent"][r]
+        rs, rt, rp = ref["cand_score64"][r], ref["cand_token"][r], ref["cand_parent"][r]
+        # canonical order inside the GPU list
+        fin = np.isfinite(gs)
+        if fin.sum() > 1:
+            d = np.diff(gs[fin].astype(np.float64))
+            assert (d <= 0).all(), f"request {r}: GPU candidates not sorted"
+        gset = {(int(p), int(t)): float(s) for s, t, p in zip(gs, gt, gp) if p >= 0}
+        rset = {(int(p), int(t)): float(s) for s, t, p in zip(rs, rt, rp) if p >= 0}
+        assert len(gset) == len(rset), f"request {r}: {len(gset)} vs {len(rset)} candidates"
+        finite_ref = [s for s in rset.values() if np.isfinite(s)]
+        boundary = min(finite_ref) if finite_ref else -np.inf
+        for key in set(gset) ^ set(rset):
+            s = gset.get(key, rset.get(key))
+            tol = rel_tol * max(1.0, abs(boundary))
+            assert np.isfinite(s) and abs(s - boundary) <= tol, \
+                f"request {r}: candidate {key} (score {s}) differs, boundary {boundary}"
+            near_ties += 1
+        for key in set(gset) & set(rset):
+            a, b = gset[key], rset[key]
+            if np.isfinite(b):
+                assert abs(a - b) <= rel_tol * max(1.0, abs(b)), f"request {r} {key}: score {a} vs {b}"
+            else:
+                assert a == b, f"request {r} {key}: score {a} vs {b}"
+    # lse against the float64 normaliser
+    gl, rl = gpu["lse"].astype(np.float64), ref["lse"].astype(np.float64)
+    fin = np.isfinite(rl)
+    assert np.all(np.abs(gl[fin] - rl[fin]) <= 1e-5 * np.maximum(1.0, np.abs(rl[fin]))), "lse mismatch"
+    return near_ties
+
+
+def assert_step_parity(case: Case, gpu: dict):
+    """Both parity levels: bit-exact given the device lse, and reference
+    arithmetic within tolerance."""
+    assert gpu["err"] == 0, f"device error word {gpu['err']:#x}"
+    exact = oracle_step(case, arith="device", lse_override=gpu["lse"])
+    assert_bit_exact(gpu, exact)
+    ref = oracle_step(case, arith="reference")
+    tol = 1e-5 if case.dtype == "f32" else 2e-3
+    return assert_close_selection(gpu, ref, rel_tol=tol, case=case)
+
+
+def next_inputs(case: Case, gpu: dict, logits32_next: np.ndarray) -> Case:
+    """Carry the GPU step's new beams into the next step's inputs."""
+    import copy
+    nc = copy.copy(case)
+    nc.logits32 = logits32_next
+    nc.cum = gpu["sel_score"].astype(np.float32)
+    nc.node = gpu["sel_node"].astype(np.int32)
+    nc.hist = gpu["hist_out"].astype(np.int32)
+    return nc
+
+
+def tiny_catalog_csr(seqs):
+    return csr_from_sequences(seqs)

@@ -1,0 +1,1184 @@
+// gr_beam_step.cu — fused constrained beam-search step for B200 (sm_100a).
+//
+// One persistent CTA per SM walks a strided list of logit rows (one row =
+// one beam of one request).  For each row it
+//   (a) streams the row through a ring of shared-memory stages filled by
+//       cp.async.bulk (TMA bulk copies, one elected thread, mbarrier
+//       completion) while all 512 threads keep an online max / sum-exp
+//       (vLLM's full-vocab log_softmax normaliser, sampler.py:300-301);
+//   (b) keeps a shared-memory copy of the token window that holds the row's
+//       trie children (constrained beams), or a thresholded top-k of the
+//       streamed values (unconstrained / reference-literal beams);
+//   (c) after the row's log-sum-exp is known, scores its candidates
+//       score = cum + (y - lse) (serving_engine.py:511, 533), drops those
+//       below the request's running 2B-th best key, selects at most 2B and
+//       appends them to the request's candidate buffer;
+//   (d) the CTA that finishes a request's last row merges the request's
+//       candidates into the canonical top-2B, the new beams (parent, token,
+//       child node) and the forked token table (serving_engine.py:566-590).
+// No CTA ever waits for another one; every mbarrier wait is bounded.
+
+#include <cstdint>
+#include <cstdio>
+#include <cuda_runtime.h>
+
+#include "../../include/gr_beam.h"
+#include "gr_device.cuh"
+
+namespace gr {
+
+constexpr int kModeProcessed = 1;
+
+struct Params {
+  // descriptor
+  int R, NB, B, V, VL, voff;
+  long long row_stride;
+  int mode, K, eos, T, N;
+  // inputs
+  const void* logits;
+  const float* cum;
+  const int* node;
+  const long long* row_ptr;
+  const int* child_tok;
+  const int* child_node;
+  const float* temp;
+  const float* rep;
+  const float* pres;
+  const float* freq;
+  const int* hist;
+  // outputs
+  float* cand_score;
+  int* cand_token;
+  int* cand_parent;
+  float* sel_score;
+  int* sel_token;
+  int* sel_parent;
+  int* sel_node;
+  float* eos_score;
+  int* hist_out;
+  float* lse_out;
+  int* err;
+  // workspace
+  unsigned long long* tau;     // [R] running lower bound of the request's 2B-th key
+  unsigned int* cnt;           // [R] keys appended
+  unsigned int* done;          // [R] rows finished
+  unsigned long long* buf;     // [R][cap]
+  long long cap;
+  // derived
+  int k2;        // 2B candidates
+  int kk;        // streamed keep count: max(2B, K) + slack
+  int pen;       // penalty pointers present
+  int stages;
+  int bm_words;
+  int partial_only;   // 1: write (max, sumexp) partials only (vocab-sharded phase 1)
+  float2* partials;
+};
+
+// Shared-memory carve-up (dynamic shared memory, 128-byte aligned pieces).
+struct Smem {
+  unsigned char* ring;
+  uint64_t* keys;
+  float* win;
+  uint32_t* bitmap;
+  int* tab_tok;
+  float* tab_xp;
+  float* tab_y;
+  SelectScratch* sel;
+  float* red_m;
+  float* red_s;
+  uint64_t* bars;
+  struct Scalars {
+    uint32_t cnt;
+    uint32_t ntab;
+    int overflow;
+    int abort;
+    int last;
+    int discard;
+    uint32_t base;
+    float lse;
+    float m_tot;
+    float s_tot;
+    float thr_y;
+    uint64_t thr_key;
+    uint64_t min_key;
+  } * v;
+};
+
+__host__ __device__ inline size_t align128(size_t x) { return (x + 127) & ~size_t(127); }
+
+__host__ __device__ inline size_t smem_bytes(int stages, int bm_words, int pen) {
+  size_t o = 0;
+  o += align128(size_t(stages) * kStageBytes);
+  o += align128(size_t(kKeyCap) * 8);
+  o += align128(size_t(kWin) * 4);
+  if (pen) {
+    o += align128(size_t(bm_words) * 4);
+    o += align128(size_t(kPenTableMax) * 12);
+  }
+  o += align128(sizeof(SelectScratch));
+  o += align128(kWarps * 8);
+  o += align128(kMaxStages * 8);
+  o += align128(sizeof(Smem::Scalars));
+  return o;
+}
+
+__device__ inline Smem carve(unsigned char* base, const Params& P) {
+  Smem S;
+  size_t o = 0;
+  S.ring = base + o; o += align128(size_t(P.stages) * kStageBytes);
+  S.keys = reinterpret_cast<uint64_t*>(base + o); o += align128(size_t(kKeyCap) * 8);
+  S.win = reinterpret_cast<float*>(base + o); o += align128(size_t(kWin) * 4);
+  if (P.pen) {
+    S.bitmap = reinterpret_cast<uint32_t*>(base + o); o += align128(size_t(P.bm_words) * 4);
+    S.tab_tok = reinterpret_cast<int*>(base + o);
+    S.tab_xp = reinterpret_cast<float*>(base + o + kPenTableMax * 4);
+    S.tab_y = reinterpret_cast<float*>(base + o + kPenTableMax * 8);
+    o += align128(size_t(kPenTableMax) * 12);
+  } else {
+    S.bitmap = nullptr; S.tab_tok = nullptr; S.tab_xp = nullptr; S.tab_y = nullptr;
+  }
+  S.sel = reinterpret_cast<SelectScratch*>(base + o); o += align128(sizeof(SelectScratch));
+  S.red_m = reinterpret_cast<float*>(base + o);
+  S.red_s = reinterpret_cast<float*>(base + o + kWarps * 4);
+  o += align128(kWarps * 8);
+  S.bars = reinterpret_cast<uint64_t*>(base + o); o += align128(kMaxStages * 8);
+  S.v = reinterpret_cast<Smem::Scalars*>(base + o);
+  return S;
+}
+
+// Row geometry: [0, head) and [tail_start, VL) are read with plain loads; the
+// 16-byte aligned body in between goes through the bulk-copy ring.
+struct Geom {
+  const char* rowp;
+  const char* body;
+  long long body_bytes;
+  int head;
+  int tail_start;
+  int nchunks;
+};
+
+template <int ES>
+__device__ __forceinline__ Geom row_geom(const Params& P, int row) {
+  Geom g;
+  g.rowp = static_cast<const char*>(P.logits) + static_cast<size_t>(row) * static_cast<size_t>(P.row_stride) * ES;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(g.rowp);
+  const uintptr_t e = a + static_cast<uintptr_t>(P.VL) * ES;
+  const uintptr_t a0 = (a + 15) & ~uintptr_t(15);
+  const uintptr_t a1 = e & ~uintptr_t(15);
+  if (a1 <= a0) {
+    g.body = g.rowp;
+    g.body_bytes = 0;
+    g.head = P.VL;
+    g.tail_start = P.VL;
+    g.nchunks = 0;
+  } else {
+    g.body = reinterpret_cast<const char*>(a0);
+    g.body_bytes = static_cast<long long>(a1 - a0);
+    g.head = static_cast<int>((a0 - a) / ES);
+    g.tail_start = static_cast<int>((a1 - a) / ES);
+    g.nchunks = static_cast<int>((g.body_bytes + kStageBytes - 1) / kStageBytes);
+  }
+  return g;
+}
+
+__device__ __forceinline__ int row_of_iter(const Params& P, int it) {
+  // b-major order: the first rows every CTA takes are the requests' best beams,
+  // which raise the per-request thresholds early.
+  const int seq = blockIdx.x + it * gridDim.x;
+  const int b = seq / P.R;
+  const int r = seq - b * P.R;
+  return r * P.NB + b;
+}
+
+__device__ __forceinline__ float eff_temperature(const Params& P, int r) {
+  if (P.temp == nullptr) return 1.0f;
+  const float t = P.temp[r];
+  return (t < 1e-5f) ? 1.0f : t;
+}
+
+// vLLM penalties for one token seen `cnt` times in the output history
+// (model_executor/layers/utils.py:51-89): repetition, then frequency, then
+// presence, each rounded to float32 (no fused multiply-add).
+__device__ __forceinline__ float penalise(float x, int cnt, float rep, float pres, float freq) {
+  x = (x > 0.0f) ? __fdiv_rn(x, rep) : __fmul_rn(x, rep);
+  x = __fsub_rn(x, __fmul_rn(freq, static_cast<float>(cnt)));
+  x = __fsub_rn(x, pres);
+  return x;
+}
+
+struct RowCtx {
+  int row, r, b, node;
+  int c0, c1;          // CSR edge range of the node (c0 == c1: none)
+  int wlo, whi;        // window [wlo, whi] in local columns (empty if wlo > whi)
+  bool stream;         // unconstrained or reference-literal
+  bool constrained;
+  bool pen_active;     // penalty table in use for this row
+  bool excl;           // processed mode: penalised tokens come from the table
+  float teff, rteff;
+  float rep, pres, freq;
+  float cum;
+};
+
+template <typename TL>
+struct Step {
+  using Tr = LogitTraits<TL>;
+  static constexpr int ES = sizeof(TL);
+  static constexpr int EPV = Tr::kPerVec;
+
+  const Params& P;
+  Smem& S;
+  __device__ Step(const Params& p, Smem& s) : P(p), S(s) {}
+
+  __device__ __forceinline__ float load_logit(const RowCtx& c, int tl) const {
+    const TL* rowp = reinterpret_cast<const TL*>(static_cast<const char*>(P.logits) +
+                                                 static_cast<size_t>(c.row) * static_cast<size_t>(P.row_stride) * ES);
+    return Tr::load1(rowp + tl);
+  }
+
+  __device__ __forceinline__ bool flagged(const RowCtx& c, int tl) const {
+    return c.pen_active && ((S.bitmap[tl >> 5] >> (tl & 31)) & 1u);
+  }
+
+  __device__ __forceinline__ int table_find(int tl) const {
+    const int n = static_cast<int>(S.v->ntab);
+    for (int j = 0; j < n; ++j)
+      if (S.tab_tok[j] == tl) return j;
+    return -1;
+  }
+
+  // Exact value in the log-prob domain for local column tl whose raw logit is x.
+  __device__ __forceinline__ float exact_y(const RowCtx& c, float x, int tl) const {
+    if (P.mode == kModeProcessed) {
+      if (c.excl && flagged(c, tl)) {
+        const int j = table_find(tl);
+        if (j >= 0) return S.tab_y[j];
+      }
+      return (c.teff == 1.0f) ? x : __fdiv_rn(x, c.teff);
+    }
+    return x;
+  }
+
+  // ---- per-element streaming work ----------------------------------------
+  // Online (max, sumexp) update with n values; -inf values contribute nothing.
+  template <int N>
+  __device__ __forceinline__ void lse_update(const float* y, float& m, float& s) const {
+    float vmax = y[0];
+#pragma unroll
+    for (int i = 1; i < N; ++i) vmax = fmaxf(vmax, y[i]);
+    if (vmax > m) {
+      s = s * fast_exp2((m - vmax) * kLog2e);
+      m = vmax;
+    }
+    if (m > -kInf) {
+      const float mb = m * kLog2e;
+#pragma unroll
+      for (int i = 0; i < N; ++i) s += fast_exp2(fmaf(y[i], kLog2e, -mb));
+    }
+  }
+
+  // Process N consecutive columns starting at local column tb (x = raw values,
+  // valid = lane holds real data).  Warp-uniform call.
+  template <int N>
+  __device__ __forceinline__ void process(const RowCtx& c, const float* x, int tb, bool valid, float& m, float& s,
+                                          float thr_y, uint64_t thr_key) const {
+    float y[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) y[i] = (P.mode == kModeProcessed) ? x[i] * c.rteff : x[i];
+    uint32_t fl = 0;
+    if (c.excl && valid) {
+      const int w = tb >> 5, sh = tb & 31;
+      uint64_t bits = S.bitmap[w];
+      if (w + 1 < P.bm_words) bits |= static_cast<uint64_t>(S.bitmap[w + 1]) << 32;
+      fl = static_cast<uint32_t>(bits >> sh) & ((N >= 32) ? 0xFFFFFFFFu : ((1u << N) - 1u));
+      if (fl) {
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+          if ((fl >> i) & 1u) y[i] = -kInf;
+      }
+    }
+    if (valid) {
+      lse_update<N>(y, m, s);
+      if (c.constrained && tb + N > c.wlo && tb <= c.whi) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          const int tl = tb + i;
+          if (tl >= c.wlo && tl <= c.whi) S.win[tl - c.wlo] = x[i];
+        }
+      }
+    }
+    if (c.stream) {
+      bool any = false;
+#pragma unroll
+      for (int i = 0; i < N; ++i) any |= valid && !((fl >> i) & 1u) && (y[i] >= thr_y);
+      if (__any_sync(0xFFFFFFFFu, any)) {
+        const uint32_t fbase = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V) +
+                               static_cast<uint32_t>(P.voff + tb);
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          bool pred = valid && !((fl >> i) & 1u) && (y[i] >= thr_y);
+          uint64_t key = 0;
+          if (pred) {
+            const float ye = (P.mode == kModeProcessed && c.teff != 1.0f) ? __fdiv_rn(x[i], c.teff) : x[i];
+            key = make_key(ye, fbase + i);
+            pred = key >= thr_key;
+          }
+          warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
+        }
+      }
+    }
+  }
+
+  // ---- selection helpers ------------------------------------------------------
+  // Reduce the shared key list to its best k (k < cnt).  Returns the cut.
+  __device__ Cut shrink_to(int k) {
+    const int n = min(static_cast<int>(S.v->cnt), kKeyCap);
+    uint64_t* keys = S.keys;
+    Cut cut = cta_radix_select([keys](int i) { return keys[i]; }, n, k, S.sel);
+    cta_compact(S.keys, n, cut, &S.v->cnt);
+    return cut;
+  }
+
+  __device__ void raise_tau(int r, uint64_t floor_key) {
+    if (threadIdx.x == 0) {
+      atomicMax(P.tau + r, static_cast<unsigned long long>(floor_key));
+      if (floor_key > S.v->thr_key) S.v->thr_key = floor_key;
+    }
+    __syncthreads();
+  }
+
+  __device__ uint64_t min_key_of_list() {
+    const int n = min(static_cast<int>(S.v->cnt), kKeyCap);
+    uint64_t mn = ~0ull;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) mn = (S.keys[i] < mn) ? S.keys[i] : mn;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t v = __shfl_xor_sync(0xFFFFFFFFu, mn, o);
+      mn = v < mn ? v : mn;
+    }
+    if (threadIdx.x == 0) S.v->min_key = ~0ull;
+    __syncthreads();
+    if (lane_id() == 0) atomicMin(reinterpret_cast<unsigned long long*>(&S.v->min_key), mn);
+    __syncthreads();
+    const uint64_t res = S.v->min_key;
+    __syncthreads();
+    return res;
+  }
+
+  // ---- row-end candidate formation -----------------------------------------
+  __device__ void constrained_candidates(const RowCtx& c, float lse) {
+    const int lane = lane_id();
+    for (int base = c.c0; base < c.c1; base += kBatch) {
+      const int end = min(base + kBatch, c.c1);
+      const uint64_t thr = S.v->thr_key;
+      for (int jb = base + warp_id() * 32; jb < end; jb += blockDim.x) {
+        const int j = jb + lane;
+        bool pred = false;
+        uint64_t key = 0;
+        if (j < end) {
+          const int tok = P.child_tok[j];
+          if (tok < 0 || tok >= P.V) {
+            atomicOr(P.err, GR_DEVERR_BAD_CHILD);
+          } else {
+            const int tl = tok - P.voff;
+            if (tl >= 0 && tl < P.VL) {
+              const float x = (tl >= c.wlo && tl <= c.whi) ? S.win[tl - c.wlo] : load_logit(c, tl);
+              const float y = exact_y(c, x, tl);
+              float sc = __fadd_rn(c.cum, __fsub_rn(y, lse));
+              if (tok == P.eos) {
+                if (P.eos_score) P.eos_score[c.row] = sc;
+                sc = -kInf;
+              }
+              key = make_key(sc, static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V) + static_cast<uint32_t>(tok));
+              pred = key >= thr;
+            }
+          }
+        }
+        warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
+      }
+      __syncthreads();
+      if (end < c.c1 && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
+        const Cut cut = shrink_to(P.k2);
+        raise_tau(c.r, cut.floor_key());
+      }
+    }
+    if (static_cast<int>(S.v->cnt) > P.k2) {
+      const Cut cut = shrink_to(P.k2);
+      raise_tau(c.r, cut.floor_key());
+    }
+  }
+
+  // Streamed rows: convert the kept value-keys (ord(y) | ~flat) into score keys.
+  // Returns false if the streamed boundary could hide a candidate.
+  __device__ void unconstrained_candidates(const RowCtx& c, float lse) {
+    // the kept set holds the row's best kk value-keys (all of them if nothing was discarded)
+    if (static_cast<int>(S.v->cnt) > P.kk) {
+      shrink_to(P.kk);
+      if (threadIdx.x == 0) S.v->discard = 1;
+      __syncthreads();
+    }
+    const bool discarded = S.v->discard != 0;
+    float y_last = -kInf;
+    if (discarded) y_last = key_score(min_key_of_list());
+    const int n = min(static_cast<int>(S.v->cnt), kKeyCap);
+    const uint32_t vb = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint64_t k = S.keys[i];
+      const uint32_t flat = key_flat(k);
+      const int tok = static_cast<int>(flat - vb);
+      float sc = __fadd_rn(c.cum, __fsub_rn(key_score(k), lse));
+      if (tok == P.eos) sc = -kInf;
+      S.keys[i] = make_key(sc, flat);
+    }
+    if (threadIdx.x == 0 && P.eos >= P.voff && P.eos < P.voff + P.VL && P.eos_score) {
+      const int tl = P.eos - P.voff;
+      const float y = exact_y(c, load_logit(c, tl), tl);
+      P.eos_score[c.row] = __fadd_rn(c.cum, __fsub_rn(y, lse));
+    }
+    __syncthreads();
+    if (n > P.k2) shrink_to(P.k2);
+    if (discarded && n > 0) {
+      const float s_last = __fadd_rn(c.cum, __fsub_rn(y_last, lse));
+      const float s_kth = key_score(min_key_of_list());
+      if (threadIdx.x == 0 && !(s_last < s_kth)) atomicOr(P.err, GR_DEVERR_TIE_BOUNDARY);
+    }
+  }
+
+  // Reference-literal rows: the beam's own top-K by log-prob (vLLM topk),
+  // de-duplicated against the greedy token, then masked to the catalog.
+  __device__ void literal_candidates(const RowCtx& c, float lse) {
+    if (static_cast<int>(S.v->cnt) > P.kk) {
+      shrink_to(P.kk);
+      if (threadIdx.x == 0) S.v->discard = 1;
+      __syncthreads();
+    }
+    const bool discarded = S.v->discard != 0;
+    const uint32_t vb = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V);
+    // greedy (sampled) token: argmax of the penalised logits, lowest id on ties
+    int sampled_tl = -1;
+    if (c.pen_active) {
+      // candidates: every kept non-penalised column (value = raw logit) and
+      // every penalised column (value = its penalised logit from the table)
+      const int n = min(static_cast<int>(S.v->cnt), kKeyCap);
+      uint64_t best = 0;
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int tl = static_cast<int>(key_flat(S.keys[i]) - vb) - P.voff;
+        if (flagged(c, tl)) continue;
+        const uint64_t k = make_key(load_logit(c, tl), static_cast<uint32_t>(tl));
+        best = k > best ? k : best;
+      }
+      const int nt = static_cast<int>(S.v->ntab);
+      for (int j = threadIdx.x; j < nt; j += blockDim.x) {
+        const uint64_t k = make_key(S.tab_xp[j], static_cast<uint32_t>(S.tab_tok[j]));
+        best = k > best ? k : best;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t v = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+        best = v > best ? v : best;
+      }
+      if (threadIdx.x == 0) S.v->min_key = 0;
+      __syncthreads();
+      if (lane_id() == 0) atomicMax(reinterpret_cast<unsigned long long*>(&S.v->min_key), best);
+      __syncthreads();
+      sampled_tl = (S.v->min_key == 0) ? -1 : static_cast<int>(key_flat(S.v->min_key));
+      __syncthreads();
+    }
+    // value keys -> log-prob keys (ties: lower token first)
+    float y_last = -kInf;
+    if (discarded) y_last = key_score(min_key_of_list());
+    int n = min(static_cast<int>(S.v->cnt), kKeyCap);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint64_t k = S.keys[i];
+      S.keys[i] = make_key(__fsub_rn(key_score(k), lse), key_flat(k));
+    }
+    __syncthreads();
+    const int K = min(P.K, n);
+    if (n > K) shrink_to(K);
+    n = min(static_cast<int>(S.v->cnt), kKeyCap);
+    const uint64_t kth = (n > 0) ? min_key_of_list() : 0ull;
+    if (discarded && n > 0) {
+      if (threadIdx.x == 0 && !(__fsub_rn(y_last, lse) < key_score(kth))) atomicOr(P.err, GR_DEVERR_TIE_BOUNDARY);
+    }
+    // dedup against the sampled token (vllm_gr/logprobs.py:47-52)
+    if (sampled_tl >= 0) {
+      const uint32_t sflat = vb + static_cast<uint32_t>(P.voff + sampled_tl);
+      if (threadIdx.x == 0) S.v->last = 0;
+      __syncthreads();
+      for (int i = threadIdx.x; i < n; i += blockDim.x)
+        if (key_flat(S.keys[i]) == sflat) S.v->last = 1;
+      __syncthreads();
+      if (S.v->last == 0 && n > 0) {
+        // replace the K-th (smallest) entry by the sampled token
+        const float ys = exact_y(c, load_logit(c, sampled_tl), sampled_tl);
+        const uint64_t sk = make_key(__fsub_rn(ys, lse), sflat);
+        for (int i = threadIdx.x; i < n; i += blockDim.x)
+          if (S.keys[i] == kth) S.keys[i] = sk;
+      }
+      __syncthreads();
+    }
+    // catalog mask, cum add, EOS (serving_engine.py:504-506, 511, 541-562)
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint64_t k = S.keys[i];
+      const uint32_t flat = key_flat(k);
+      const int tok = static_cast<int>(flat - vb);
+      bool allowed = true;
+      if (c.node >= 0) {
+        int lo = c.c0, hi = c.c1;
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (P.child_tok[mid] < tok) lo = mid + 1; else hi = mid;
+        }
+        allowed = (lo < c.c1) && (P.child_tok[lo] == tok);
+      } else if (c.node == GR_NODE_DEAD) {
+        allowed = false;
+      }
+      float sc = allowed ? __fadd_rn(c.cum, key_score(k)) : -kInf;
+      if (tok == P.eos) {
+        if (P.eos_score) P.eos_score[c.row] = sc;
+        sc = -kInf;
+      }
+      S.keys[i] = make_key(sc, flat);
+    }
+    __syncthreads();
+    if (n > P.k2) shrink_to(P.k2);
+  }
+
+  // Append the row's keys that beat the request threshold; returns nothing.
+  __device__ void emit(const RowCtx& c) {
+    if (threadIdx.x == 0) {
+      const uint64_t t = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
+      if (t > S.v->thr_key) S.v->thr_key = t;
+    }
+    __syncthreads();
+    const uint64_t thr = S.v->thr_key;
+    int n = min(static_cast<int>(S.v->cnt), kKeyCap);
+    if (thr > 0 && n > 0) n = static_cast<int>(cta_compact(S.keys, n, Cut{thr, 0}, &S.v->cnt));
+    if (threadIdx.x == 0) S.v->base = n > 0 ? atomicAdd(P.cnt + c.r, static_cast<unsigned>(n)) : 0u;
+    __syncthreads();
+    const long long base = S.v->base;
+    if (threadIdx.x == 0 && base + n > P.cap) atomicOr(P.err, GR_DEVERR_OVERFLOW);
+    unsigned long long* dst = P.buf + static_cast<size_t>(c.r) * static_cast<size_t>(P.cap);
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+      if (base + i < P.cap) dst[base + i] = S.keys[i];
+  }
+
+  // The last CTA of request r: canonical top-2B, new beams and fork table.
+  __device__ void merge_request(int r) {
+    const unsigned long long* src = P.buf + static_cast<size_t>(r) * static_cast<size_t>(P.cap);
+    int n = static_cast<int>(*reinterpret_cast<volatile unsigned*>(P.cnt + r));
+    if (n > P.cap) n = static_cast<int>(P.cap);
+    const int k = min(P.k2, n);
+    if (threadIdx.x == 0) S.v->cnt = 0;
+    __syncthreads();
+    if (n > k) {
+      const Cut cut = cta_radix_select([src](int i) { return __ldcg(src + i); }, n, k, S.sel);
+      int dummy = 0;
+      for (int ib = warp_id() * 32; ib < n; ib += blockDim.x) {
+        const int i = ib + lane_id();
+        uint64_t key = 0;
+        bool pred = false;
+        if (i < n) {
+          key = __ldcg(src + i);
+          pred = cut.keep(key);
+        }
+        warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &dummy);
+      }
+    } else {
+      for (int i = threadIdx.x; i < n; i += blockDim.x) S.keys[i] = __ldcg(src + i);
+    }
+    __syncthreads();
+    int P2 = 1;
+    while (P2 < k) P2 <<= 1;
+    for (int i = k + threadIdx.x; i < P2; i += blockDim.x) S.keys[i] = 0ull;
+    __syncthreads();
+    cta_bitonic_sort_desc(S.keys, P2);
+    const int B = P.B, k2 = P.k2, NB = P.NB, T = P.T;
+    for (int i = threadIdx.x; i < k2; i += blockDim.x) {
+      float sc = -kInf;
+      int tok = -1, par = -1;
+      if (i < k) {
+        const uint64_t key = S.keys[i];
+        const uint32_t flat = key_flat(key);
+        sc = key_score(key);
+        tok = static_cast<int>(flat % static_cast<uint32_t>(P.V));
+        par = static_cast<int>(flat / static_cast<uint32_t>(P.V));
+      }
+      P.cand_score[static_cast<size_t>(r) * k2 + i] = sc;
+      P.cand_token[static_cast<size_t>(r) * k2 + i] = tok;
+      P.cand_parent[static_cast<size_t>(r) * k2 + i] = par;
+      if (i < B) {
+        P.sel_score[static_cast<size_t>(r) * B + i] = sc;
+        P.sel_token[static_cast<size_t>(r) * B + i] = tok;
+        P.sel_parent[static_cast<size_t>(r) * B + i] = par;
+        int child = GR_NODE_DEAD;
+        if (par >= 0) {
+          const int pn = P.node[r * NB + par];
+          if (pn == GR_NODE_UNCONSTRAINED) {
+            child = GR_NODE_UNCONSTRAINED;
+          } else if (pn >= 0 && pn < P.N) {
+            int lo = static_cast<int>(P.row_ptr[pn]);
+            const int hi0 = static_cast<int>(P.row_ptr[pn + 1]);
+            int hi = hi0;
+            while (lo < hi) {
+              const int mid = (lo + hi) >> 1;
+              if (P.child_tok[mid] < tok) lo = mid + 1; else hi = mid;
+            }
+            if (lo < hi0 && P.child_tok[lo] == tok) child = P.child_node[lo];
+          }
+        }
+        P.sel_node[static_cast<size_t>(r) * B + i] = child;
+      }
+    }
+    if (P.hist_out) {
+      const int W = T + 1;
+      for (int idx = threadIdx.x; idx < B * W; idx += blockDim.x) {
+        const int i = idx / W, t = idx - i * W;
+        int v = -1;
+        if (i < k) {
+          const uint32_t flat = key_flat(S.keys[i]);
+          const int par = static_cast<int>(flat / static_cast<uint32_t>(P.V));
+          v = (t < T) ? P.hist[(static_cast<size_t>(r) * NB + par) * T + t]
+                      : static_cast<int>(flat % static_cast<uint32_t>(P.V));
+        }
+        P.hist_out[static_cast<size_t>(r) * B * W + idx] = v;
+      }
+    }
+    __syncthreads();
+  }
+};
+
+template <typename TL>
+__global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_constant__ Params P) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  Smem S = carve(smem_raw, P);
+  Step<TL> st(P, S);
+  using Tr = LogitTraits<TL>;
+  constexpr int ES = sizeof(TL);
+  constexpr int EPV = Tr::kPerVec;
+  constexpr int kChunkElems = kStageBytes / ES;
+  constexpr int kSubVecs = kBatch / EPV;     // vectors between capacity checks (stream rows)
+
+  const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
+  const int total = P.R * P.NB;
+  const int my_n = (static_cast<int>(blockIdx.x) < total) ? (total - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1 : 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < P.stages; ++s) mbar_init(&S.bars[s], 1);
+    fence_mbar_init();
+    S.v->abort = 0;
+  }
+  if (P.pen)
+    for (int i = tid; i < P.bm_words; i += blockDim.x) S.bitmap[i] = 0u;
+  __syncthreads();
+
+  // ---- producer state (thread 0 only) ----
+  int p_it = 0, p_c = 0;
+  long long issued = 0;
+  const uint64_t pol = l2_policy_evict_first();
+  auto issue_next = [&]() {
+    while (p_it < my_n) {
+      const Geom g = row_geom<ES>(P, row_of_iter(P, p_it));
+      if (p_c < g.nchunks) {
+        const int stage = static_cast<int>(issued % P.stages);
+        const long long off = static_cast<long long>(p_c) * kStageBytes;
+        const uint32_t bytes = static_cast<uint32_t>(min(static_cast<long long>(kStageBytes), g.body_bytes - off));
+        mbar_arrive_expect_tx(&S.bars[stage], bytes);
+        bulk_copy_g2s(S.ring + static_cast<size_t>(stage) * kStageBytes, g.body + off, bytes, &S.bars[stage], pol);
+        ++issued;
+        ++p_c;
+        return;
+      }
+      ++p_it;
+      p_c = 0;
+    }
+  };
+  if (tid == 0) {
+    fence_proxy_async_smem();
+    for (int s = 0; s < P.stages; ++s) issue_next();
+  }
+
+  long long consumed = 0;
+  for (int it = 0; it < my_n; ++it) {
+    // ------------------------------------------------------------ row setup
+    RowCtx c;
+    c.row = row_of_iter(P, it);
+    c.r = c.row / P.NB;
+    c.b = c.row - c.r * P.NB;
+    c.node = P.node[c.row];
+    if (c.node < GR_NODE_DEAD || c.node >= P.N) {
+      if (tid == 0) atomicOr(P.err, GR_DEVERR_BAD_NODE);
+      c.node = GR_NODE_DEAD;
+    }
+    c.stream = (P.K > 0) || (c.node == GR_NODE_UNCONSTRAINED);
+    c.constrained = !c.stream && c.node >= 0;
+    c.c0 = c.c1 = 0;
+    if (c.node >= 0) {
+      c.c0 = static_cast<int>(P.row_ptr[c.node]);
+      c.c1 = static_cast<int>(P.row_ptr[c.node + 1]);
+    }
+    c.wlo = 1;
+    c.whi = 0;
+    if (c.constrained && c.c1 > c.c0) {
+      const int lo = max(P.child_tok[c.c0] - P.voff, 0);
+      const int hi = min(P.child_tok[c.c1 - 1] - P.voff, P.VL - 1);
+      if (lo <= hi) {
+        c.wlo = lo;
+        c.whi = min(hi, lo + kWin - 1);
+      }
+    }
+    c.cum = P.cum[c.row];
+    c.teff = (P.mode == kModeProcessed) ? eff_temperature(P, c.r) : 1.0f;
+    c.rteff = __frcp_rn(c.teff);
+    c.rep = P.rep ? P.rep[c.r] : 1.0f;
+    c.pres = P.pres ? P.pres[c.r] : 0.0f;
+    c.freq = P.freq ? P.freq[c.r] : 0.0f;
+    const bool has_pen = P.pen && P.T > 0 && !(c.rep == 1.0f && c.pres == 0.0f && c.freq == 0.0f);
+    if (P.partial_only) {
+      // vocab-sharded phase 1: only the normaliser of the local columns
+      c.stream = false;
+      c.constrained = false;
+      c.pen_active = has_pen && P.mode == kModeProcessed;
+    } else {
+      c.pen_active = has_pen && (P.mode == kModeProcessed || P.K > 0);
+    }
+    c.excl = c.pen_active && P.mode == kModeProcessed;
+
+    if (tid == 0) {
+      S.v->cnt = 0;
+      S.v->ntab = 0;
+      S.v->overflow = 0;
+      S.v->discard = 0;
+      S.v->thr_key = 0ull;
+      S.v->thr_y = -kInf;
+      if (P.eos_score && !P.partial_only) P.eos_score[c.row] = __int_as_float(0x7FC00000);
+    }
+    __syncthreads();
+    if (c.pen_active) {
+      const int* h = P.hist + static_cast<size_t>(c.row) * P.T;
+      for (int t = tid; t < P.T; t += blockDim.x) {
+        const int tok = h[t];
+        const int tl = tok - P.voff;
+        if (tok >= 0 && tl >= 0 && tl < P.VL) {
+          const uint32_t bit = 1u << (tl & 31);
+          const uint32_t old = atomicOr(&S.bitmap[tl >> 5], bit);
+          if (!(old & bit)) {
+            int cnt = 0;
+            for (int j = 0; j < P.T; ++j) cnt += (h[j] == tok);
+            const float xp = penalise(st.load_logit(c, tl), cnt, c.rep, c.pres, c.freq);
+            const uint32_t idx = atomicAdd(&S.v->ntab, 1u);
+            S.tab_tok[idx] = tl;
+            S.tab_xp[idx] = xp;
+            S.tab_y[idx] = (P.mode == kModeProcessed) ? ((c.teff == 1.0f) ? xp : __fdiv_rn(xp, c.teff)) : xp;
+          }
+        }
+      }
+      __syncthreads();
+    }
+
+    float m = -kInf, s = 0.0f;
+    float thr_y = -kInf;
+    uint64_t thr_key = 0ull;
+    const Geom g = row_geom<ES>(P, c.row);
+
+    // ------------------------------------------------------- head / tail scalars
+    {
+      const int nh = g.head, nt = P.VL - g.tail_start;
+      const int ns = nh + nt;
+      for (int ib = warp * 32; ib < ns; ib += blockDim.x) {
+        const int i = ib + lane;
+        const bool valid = i < ns;
+        const int tl = valid ? ((i < nh) ? i : g.tail_start + (i - nh)) : 0;
+        float x[1];
+        x[0] = valid ? st.load_logit(c, tl) : -kInf;
+        st.template process<1>(c, x, tl, valid, m, s, thr_y, thr_key);
+      }
+    }
+
+    // ------------------------------------------------------------ body chunks
+    for (int ch = 0; ch < g.nchunks; ++ch) {
+      const int stage = static_cast<int>(consumed % P.stages);
+      const uint32_t parity = static_cast<uint32_t>((consumed / P.stages) & 1);
+      if (!mbar_wait_bounded(&S.bars[stage], parity)) {
+        S.v->abort = 1;
+        atomicOr(P.err, GR_DEVERR_TIMEOUT);
+      }
+      const long long off = static_cast<long long>(ch) * kStageBytes;
+      const int bytes = static_cast<int>(min(static_cast<long long>(kStageBytes), g.body_bytes - off));
+      const int nvec = bytes >> 4;
+      const uint4* sv = reinterpret_cast<const uint4*>(S.ring + static_cast<size_t>(stage) * kStageBytes);
+      const int tbase = g.head + ch * kChunkElems;
+      if (!c.stream) {
+        for (int vb = warp * 32; vb < nvec; vb += blockDim.x) {
+          const int v = vb + lane;
+          const bool valid = v < nvec;
+          float x[EPV];
+          if (valid) {
+            Tr::unpack(sv[v], x);
+          } else {
+#pragma unroll
+            for (int i = 0; i < EPV; ++i) x[i] = -kInf;
+          }
+          st.template process<EPV>(c, x, tbase + v * EPV, valid, m, s, thr_y, thr_key);
+        }
+      } else {
+        for (int sb = 0; sb < nvec; sb += kSubVecs) {
+          const int send = min(nvec, sb + kSubVecs);
+          for (int vb = sb + warp * 32; vb < send; vb += blockDim.x) {
+            const int v = vb + lane;
+            const bool valid = v < send;
+            float x[EPV];
+            if (valid) {
+              Tr::unpack(sv[v], x);
+            } else {
+#pragma unroll
+              for (int i = 0; i < EPV; ++i) x[i] = -kInf;
+            }
+            st.template process<EPV>(c, x, tbase + v * EPV, valid, m, s, thr_y, thr_key);
+          }
+          __syncthreads();
+          if (static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
+            const Cut cut = st.shrink_to(P.kk);
+            if (tid == 0) {
+              S.v->discard = 1;
+              S.v->thr_key = cut.floor_key();
+              const float ty = key_score(cut.floor_key());
+              S.v->thr_y = ty - fabsf(ty) * 2.0e-6f - 1e-30f;
+            }
+            __syncthreads();
+            thr_key = S.v->thr_key;
+            thr_y = S.v->thr_y;
+          }
+        }
+      }
+      __syncthreads();
+      if (S.v->abort) goto drain;
+      if (tid == 0) {
+        fence_proxy_async_smem();
+        issue_next();
+      }
+      ++consumed;
+    }
+
+    // ------------------------------------------------------------ row end
+    if (c.excl) {
+      // penalised tokens were left out of the stream; add their exact values
+      const int nt = static_cast<int>(S.v->ntab);
+      for (int jb = warp * 32; jb < nt; jb += blockDim.x) {
+        const int j = jb + lane;
+        const bool valid = j < nt;
+        float y[1];
+        y[0] = valid ? S.tab_y[j] : -kInf;
+        if (valid) st.template lse_update<1>(y, m, s);
+        if (c.stream) {
+          bool pred = false;
+          uint64_t key = 0;
+          if (valid) {
+            key = make_key(y[0], static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V) +
+                                     static_cast<uint32_t>(P.voff + S.tab_tok[j]));
+            pred = key >= thr_key;
+          }
+          warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
+        }
+      }
+    }
+    // CTA reduction of (m, s)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xFFFFFFFFu, m, o);
+      const float s2 = __shfl_xor_sync(0xFFFFFFFFu, s, o);
+      const float M = fmaxf(m, m2);
+      if (M == -kInf) {
+        s = 0.0f;
+      } else {
+        s = s * fast_exp2((m - M) * kLog2e) + s2 * fast_exp2((m2 - M) * kLog2e);
+      }
+      m = M;
+    }
+    if (lane == 0) {
+      S.red_m[warp] = m;
+      S.red_s[warp] = s;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float M = -kInf;
+      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, S.red_m[w]);
+      float tot = 0.0f;
+      if (M > -kInf)
+        for (int w = 0; w < kWarps; ++w) tot += S.red_s[w] * fast_exp2((S.red_m[w] - M) * kLog2e);
+      S.v->m_tot = M;
+      S.v->s_tot = tot;
+      S.v->lse = M + logf(tot);
+      if (P.lse_out) P.lse_out[c.row] = S.v->lse;
+      if (P.partial_only) P.partials[c.row] = make_float2(M, tot);
+    }
+    __syncthreads();
+    const float lse = S.v->lse;
+
+    if (!P.partial_only) {
+      if (c.constrained) {
+        if (tid == 0) S.v->thr_key = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
+        __syncthreads();
+        st.constrained_candidates(c, lse);
+      } else if (c.stream && P.K == 0) {
+        st.unconstrained_candidates(c, lse);
+      } else if (c.stream) {
+        st.literal_candidates(c, lse);
+      }
+      if (tid == 0 && S.v->overflow) atomicOr(P.err, GR_DEVERR_OVERFLOW);
+      if (c.stream) {
+        // the row-local threshold was over value keys; only the request bound applies now
+        if (tid == 0) S.v->thr_key = 0ull;
+        __syncthreads();
+      }
+      st.emit(c);
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) {
+        const unsigned prev = atomicAdd(P.done + c.r, 1u);
+        S.v->last = (prev == static_cast<unsigned>(P.NB - 1)) ? 1 : 0;
+      }
+      __syncthreads();
+      if (S.v->last) {
+        __threadfence();
+        st.merge_request(c.r);
+      }
+    }
+    if (c.pen_active) {
+      const int nt = static_cast<int>(S.v->ntab);
+      for (int j = tid; j < nt; j += blockDim.x) S.bitmap[S.tab_tok[j] >> 5] = 0u;
+    }
+    __syncthreads();
+  }
+  return;
+
+drain:
+  // A bounded wait ran out: wait (bounded) for this CTA's copies still in
+  // flight so that none lands after the CTA has exited, then leave.
+  if (tid == 0) {
+    for (long long q = consumed; q < issued; ++q) {
+      const int stage = static_cast<int>(q % P.stages);
+      mbar_wait_bounded(&S.bars[stage], static_cast<uint32_t>((q / P.stages) & 1));
+    }
+  }
+  __syncthreads();
+}
+
+// ============================================================== host side
+struct DeviceInfo {
+  int sms = 0;
+  int smem_optin = 0;
+  int major = 0;
+  bool attr_set[3] = {false, false, false};
+};
+
+static DeviceInfo g_dev[64];
+
+static int device_info(DeviceInfo** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GR_ERR_NO_DEVICE;
+  if (dev < 0 || dev >= 64) return GR_ERR_NO_DEVICE;
+  DeviceInfo& d = g_dev[dev];
+  if (d.sms == 0) {
+    int sms = 0, smem = 0, major = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return GR_ERR_CUDA;
+    if (cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return GR_ERR_CUDA;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return GR_ERR_CUDA;
+    d.smem_optin = smem;
+    d.major = major;
+    d.sms = sms;
+  }
+  if (d.major != 10) return GR_ERR_NO_DEVICE;
+  *out = &d;
+  return GR_OK;
+}
+
+static size_t ws_header_bytes(int R) { return align128(size_t(R) * 16); }
+
+static int validate(const gr_step_desc* d) {
+  if (!d) return GR_ERR_NULL;
+  if (d->num_requests < 1 || d->num_beams < 1 || d->beam_width < 1) return GR_ERR_BAD_DESC;
+  if (d->vocab_size < 1 || d->vocab_local < 1 || d->vocab_offset < 0) return GR_ERR_BAD_DESC;
+  if (static_cast<long long>(d->vocab_offset) + d->vocab_local > d->vocab_size) return GR_ERR_BAD_DESC;
+  if (d->row_stride < d->vocab_local) return GR_ERR_BAD_DESC;
+  if (d->logit_dtype < GR_DTYPE_F32 || d->logit_dtype > GR_DTYPE_F16) return GR_ERR_DTYPE;
+  if (d->logprobs_mode != GR_LOGPROBS_RAW && d->logprobs_mode != GR_LOGPROBS_PROCESSED) return GR_ERR_DTYPE;
+  if (d->per_beam_k < 0 || d->per_beam_k > d->vocab_local) return GR_ERR_BAD_DESC;
+  if (d->hist_len < 0 || d->num_nodes < 0 || d->num_edges < 0) return GR_ERR_BAD_DESC;
+  if (d->eos_token_id < -1 || d->eos_token_id >= d->vocab_size) return GR_ERR_BAD_DESC;
+  // flat index parent*V + token must fit in 32 bits
+  if (static_cast<unsigned long long>(d->num_beams) * static_cast<unsigned long long>(d->vocab_size) >
+      0xFFFFFFFFull)
+    return GR_ERR_UNSUPPORTED;
+  // shared-memory key list: 2B (+ streamed slack) must fit beside one batch
+  const int k2 = 2 * d->beam_width;
+  if (k2 > kKeyCap / 2) return GR_ERR_UNSUPPORTED;
+  const int kk = (k2 > d->per_beam_k ? k2 : d->per_beam_k) + kSlack;
+  if (kk > kKeyCap - kBatch) return GR_ERR_UNSUPPORTED;
+  if (d->num_edges > 0x7FFFFFFFll) return GR_ERR_UNSUPPORTED;
+  return GR_OK;
+}
+
+static void fill_params(Params& P, const gr_step_desc* d, const gr_step_io* io) {
+  P.R = d->num_requests;
+  P.NB = d->num_beams;
+  P.B = d->beam_width;
+  P.V = d->vocab_size;
+  P.VL = d->vocab_local;
+  P.voff = d->vocab_offset;
+  P.row_stride = d->row_stride;
+  P.mode = d->logprobs_mode;
+  P.K = d->per_beam_k;
+  P.eos = d->eos_token_id;
+  P.T = d->hist_len;
+  P.N = d->num_nodes;
+  P.logits = io->logits;
+  P.cum = io->cum;
+  P.node = io->node;
+  P.row_ptr = reinterpret_cast<const long long*>(io->row_ptr);
+  P.child_tok = io->child_tok;
+  P.child_node = io->child_node;
+  P.temp = io->temperature;
+  P.rep = io->rep_penalty;
+  P.pres = io->pres_penalty;
+  P.freq = io->freq_penalty;
+  P.hist = io->hist_in;
+  P.cand_score = io->cand_score;
+  P.cand_token = io->cand_token;
+  P.cand_parent = io->cand_parent;
+  P.sel_score = io->sel_score;
+  P.sel_token = io->sel_token;
+  P.sel_parent = io->sel_parent;
+  P.sel_node = io->sel_node;
+  P.eos_score = io->eos_score;
+  P.hist_out = io->hist_out;
+  P.lse_out = io->lse;
+  P.err = io->err;
+  P.k2 = 2 * d->beam_width;
+  P.kk = (P.k2 > P.K ? P.k2 : P.K) + kSlack;
+  P.pen = (io->rep_penalty || io->pres_penalty || io->freq_penalty) ? 1 : 0;
+  P.bm_words = (d->vocab_local + 31) / 32 + 1;
+  P.partial_only = 0;
+  P.partials = nullptr;
+}
+
+template <typename TL>
+static int launch_fused(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream_t stream) {
+  // as many ring stages as fit beside the fixed pieces
+  int stages = kMaxStages;
+  while (stages > 2 && smem_bytes(stages, P.bm_words, P.pen) > static_cast<size_t>(dev->smem_optin)) --stages;
+  const size_t smem = smem_bytes(stages, P.bm_words, P.pen);
+  if (smem > static_cast<size_t>(dev->smem_optin)) return GR_ERR_UNSUPPORTED;
+  P.stages = stages;
+  if (!dev->attr_set[dtype_idx]) {
+    if (cudaFuncSetAttribute(fused_step_kernel<TL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             dev->smem_optin) != cudaSuccess)
+      return GR_ERR_CUDA;
+    dev->attr_set[dtype_idx] = true;
+  }
+  const int total = P.R * P.NB;
+  const int grid = total < dev->sms ? total : dev->sms;
+  fused_step_kernel<TL><<<grid, kThreads, smem, stream>>>(P);
+  if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
+  return GR_OK;
+}
+
+static int launch_by_dtype(Params& P, int dtype, DeviceInfo* dev, cudaStream_t stream) {
+  switch (dtype) {
+    case GR_DTYPE_F32: return launch_fused<float>(P, dev, 0, stream);
+    case GR_DTYPE_BF16: return launch_fused<__nv_bfloat16>(P, dev, 1, stream);
+    case GR_DTYPE_F16: return launch_fused<__half>(P, dev, 2, stream);
+    default: return GR_ERR_DTYPE;
+  }
+}
+
+}  // namespace gr
+
+using namespace gr;
+
+extern "C" {
+
+int32_t gr_abi_version(void) { return GR_ABI_VERSION; }
+
+const char* gr_status_string(int32_t s) {
+  switch (s) {
+    case GR_OK: return "GR_OK";
+    case GR_ERR_NULL: return "GR_ERR_NULL";
+    case GR_ERR_BAD_DESC: return "GR_ERR_BAD_DESC";
+    case GR_ERR_DTYPE: return "GR_ERR_DTYPE";
+    case GR_ERR_MISALIGNED: return "GR_ERR_MISALIGNED";
+    case GR_ERR_WORKSPACE: return "GR_ERR_WORKSPACE";
+    case GR_ERR_UNSUPPORTED: return "GR_ERR_UNSUPPORTED";
+    case GR_ERR_CUDA: return "GR_ERR_CUDA";
+    case GR_ERR_NO_DEVICE: return "GR_ERR_NO_DEVICE";
+    default: return "GR_ERR_UNKNOWN";
+  }
+}
+
+int32_t gr_beam_step_workspace_size(const gr_step_desc* d, size_t* bytes) {
+  if (!d || !bytes) return GR_ERR_NULL;
+  const int v = validate(d);
+  if (v != GR_OK) return v;
+  const size_t cap = size_t(d->num_beams) * size_t(2 * d->beam_width);
+  *bytes = ws_header_bytes(d->num_requests) + align128(size_t(d->num_requests) * cap * 8);
+  return GR_OK;
+}
+
+int32_t gr_beam_step(const gr_step_desc* d, const gr_step_io* io, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  if (!d || !io) return GR_ERR_NULL;
+  int v = validate(d);
+  if (v != GR_OK) return v;
+  if (!io->logits || !io->cum || !io->node || !io->err) return GR_ERR_NULL;
+  if (!io->cand_score || !io->cand_token || !io->cand_parent) return GR_ERR_NULL;
+  if (!io->sel_score || !io->sel_token || !io->sel_parent || !io->sel_node) return GR_ERR_NULL;
+  if (d->num_nodes > 0 && (!io->row_ptr || !io->child_tok || !io->child_node)) return GR_ERR_NULL;
+  if (d->hist_len > 0 && !io->hist_in) return GR_ERR_NULL;
+  const bool pen = io->rep_penalty || io->pres_penalty || io->freq_penalty;
+  if (pen && d->hist_len > kPenTableMax) return GR_ERR_UNSUPPORTED;
+  if (pen && (d->vocab_local + 31) / 32 + 1 > kMaxBitmapWords) return GR_ERR_UNSUPPORTED;
+  if (!workspace) return GR_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u) return GR_ERR_MISALIGNED;
+  size_t need = 0;
+  gr_beam_step_workspace_size(d, &need);
+  if (workspace_bytes < need) return GR_ERR_WORKSPACE;
+  DeviceInfo* dev = nullptr;
+  v = device_info(&dev);
+  if (v != GR_OK) return v;
+
+  Params P;
+  fill_params(P, d, io);
+  const int R = d->num_requests;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  P.tau = reinterpret_cast<unsigned long long*>(ws);
+  P.cnt = reinterpret_cast<unsigned int*>(ws + size_t(R) * 8);
+  P.done = reinterpret_cast<unsigned int*>(ws + size_t(R) * 12);
+  P.buf = reinterpret_cast<unsigned long long*>(ws + ws_header_bytes(R));
+  P.cap = static_cast<long long>(d->num_beams) * (2 * d->beam_width);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(ws, 0, size_t(R) * 16, s) != cudaSuccess) return GR_ERR_CUDA;
+  return launch_by_dtype(P, d->logit_dtype, dev, s);
+}
+
+int32_t gr_lse_partials(const gr_step_desc* d, const void* logits, const float* temperature,
+                        const float* rep_penalty, const float* pres_penalty, const float* freq_penalty,
+                        const int32_t* hist_in, float* partials, int32_t* err, void* stream) {
+  (void)d; (void)logits; (void)temperature; (void)rep_penalty; (void)pres_penalty; (void)freq_penalty;
+  (void)hist_in; (void)partials; (void)err; (void)stream;
+  return GR_ERR_UNSUPPORTED;
+}
+
+int32_t gr_shard_candidates(const gr_step_desc* d, const gr_step_io* io, const float* gathered_partials,
+                            int32_t num_shards, uint64_t* shard_keys, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  (void)d; (void)io; (void)gathered_partials; (void)num_shards; (void)shard_keys; (void)workspace;
+  (void)workspace_bytes; (void)stream;
+  return GR_ERR_UNSUPPORTED;
+}
+
+int32_t gr_merge_candidates(const gr_step_desc* d, const gr_step_io* io, const uint64_t* gathered_keys,
+                            int32_t num_shards, void* stream) {
+  (void)d; (void)io; (void)gathered_keys; (void)num_shards; (void)stream;
+  return GR_ERR_UNSUPPORTED;
+}
+
+}  // extern "C"

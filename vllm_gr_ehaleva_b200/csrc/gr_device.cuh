@@ -1,0 +1,316 @@
+// gr_device.cuh — device building blocks of the constrained beam step (sm_100a).
+//
+//  * mbarrier + cp.async.bulk (TMA bulk copy, no tensor map, no multicast)
+//    global -> shared staging, with bounded waits that report instead of hang;
+//  * order-preserving 64-bit candidate keys: (ord(score) << 32) | ~flat, so
+//    that a larger key is a better candidate under the canonical order
+//    "score descending, then flat index parent*V+token ascending";
+//  * CTA-wide MSB-first radix select (8-bit digits, warp-aggregated shared
+//    histograms), in-place compaction and a bitonic sort of keys.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace gr {
+
+constexpr int kThreads = 512;                 // one CTA per SM, persistent
+constexpr int kWarps = kThreads / 32;
+constexpr int kStageBytes = 16384;            // one TMA bulk copy per stage
+constexpr int kMaxStages = 8;
+constexpr int kWin = 8192;                    // child-window tokens kept per row
+constexpr int kKeyCap = 8192;                 // candidate keys in shared memory
+constexpr int kBatch = 4096;                  // max insertions between capacity checks
+constexpr int kPenTableMax = 1024;            // max history tokens with penalties
+constexpr int kSlack = 64;                    // extra keys kept by streamed top-k
+constexpr int kMaxBitmapWords = 8192;         // penalties: local vocab <= 262144
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s per wait
+
+constexpr float kLog2e = 1.4426950408889634f;
+#define kInf (__int_as_float(0x7f800000))
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for the phase with the given parity to complete; false after kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// Bulk copy `bytes` (multiple of 16, both addresses 16-byte aligned) from this
+// GPU's global memory into this CTA's shared memory; completion is signalled
+// on `bar` as transaction bytes.  No cluster multicast.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// ---------------------------------------------------------------- keys
+__device__ __forceinline__ uint32_t f32_to_ord(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float ord_to_f32(uint32_t o) {
+  const uint32_t u = (o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o;
+  return __uint_as_float(u);
+}
+
+// Larger key = better candidate: higher score, then lower flat index.
+__device__ __forceinline__ uint64_t make_key(float score, uint32_t flat) {
+  score = __fadd_rn(score, 0.0f);  // -0 -> +0 so that equal scores tie
+  return (static_cast<uint64_t>(f32_to_ord(score)) << 32) | static_cast<uint64_t>(0xFFFFFFFFu - flat);
+}
+
+__device__ __forceinline__ float key_score(uint64_t k) { return ord_to_f32(static_cast<uint32_t>(k >> 32)); }
+__device__ __forceinline__ uint32_t key_flat(uint64_t k) { return 0xFFFFFFFFu - static_cast<uint32_t>(k); }
+
+// ---------------------------------------------------------------- warp helpers
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+__device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
+
+// Append `key` to keys[*cnt] for the lanes with `pred`.  Must be called by all
+// 32 lanes of the warp (warp-uniform control flow).
+__device__ __forceinline__ void warp_append(bool pred, uint64_t key, uint64_t* keys, uint32_t* cnt,
+                                            uint32_t cap, int* overflow) {
+  const unsigned bal = __ballot_sync(0xFFFFFFFFu, pred);
+  if (bal == 0) return;
+  const int lane = lane_id();
+  const int leader = __ffs(bal) - 1;
+  uint32_t base = 0;
+  if (lane == leader) base = atomicAdd(cnt, static_cast<uint32_t>(__popc(bal)));
+  base = __shfl_sync(0xFFFFFFFFu, base, leader);
+  if (pred) {
+    const uint32_t pos = base + __popc(bal & ((1u << lane) - 1u));
+    if (pos < cap)
+      keys[pos] = key;
+    else
+      *overflow = 1;
+  }
+}
+
+// ---------------------------------------------------------------- radix select
+// Keys kept by a selection: (key >> shift) >= (prefix >> shift).
+struct Cut {
+  uint64_t prefix;
+  int shift;
+  __device__ __forceinline__ bool keep(uint64_t k) const { return (k >> shift) >= (prefix >> shift); }
+  // A value every kept key is >= to (lower bound of the k-th largest key).
+  __device__ __forceinline__ uint64_t floor_key() const {
+    return shift >= 64 ? 0ull : (prefix >> shift) << shift;
+  }
+};
+
+struct SelectScratch {
+  uint32_t hist[256];
+  uint32_t digit, above, count, pad;
+};
+
+// The k largest of n distinct keys (1 <= k <= n), MSB-first over 8-bit digits.
+// keyf(i) returns key i.  All threads of the CTA call this.
+template <class KeyFn>
+__device__ Cut cta_radix_select(KeyFn keyf, int n, int k, SelectScratch* sc) {
+  uint64_t prefix = 0;
+  int shift = 64;
+  int krem = k;
+  const int lane = lane_id();
+  while (true) {
+    shift -= 8;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) sc->hist[i] = 0;
+    __syncthreads();
+    const int hs = shift + 8;
+    for (int ib = warp_id() * 32; ib < n; ib += blockDim.x) {
+      const int i = ib + lane;
+      uint32_t digit = 256u;
+      if (i < n) {
+        const uint64_t key = keyf(i);
+        const bool match = (hs >= 64) || ((key >> hs) == (prefix >> hs));
+        if (match) digit = static_cast<uint32_t>((key >> shift) & 0xFFu);
+      }
+      const unsigned peers = __match_any_sync(0xFFFFFFFFu, digit);
+      if (digit < 256u && lane == __ffs(peers) - 1) atomicAdd(&sc->hist[digit], static_cast<uint32_t>(__popc(peers)));
+    }
+    __syncthreads();
+    if (warp_id() == 0) {
+      uint32_t c[8];
+      uint32_t sum = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = sc->hist[255 - 8 * lane - j];
+        sum += c[j];
+      }
+      uint32_t inc = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if (lane >= o) inc += v;
+      }
+      const uint32_t exc = inc - sum;
+      if (exc < static_cast<uint32_t>(krem) && static_cast<uint32_t>(krem) <= inc) {
+        uint32_t acc = exc;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (acc + c[j] >= static_cast<uint32_t>(krem)) {
+            sc->digit = 255u - 8u * lane - j;
+            sc->above = acc;
+            sc->count = c[j];
+            break;
+          }
+          acc += c[j];
+        }
+      }
+    }
+    __syncthreads();
+    const uint32_t d = sc->digit, above = sc->above, cnt = sc->count;
+    __syncthreads();
+    prefix |= static_cast<uint64_t>(d) << shift;
+    krem -= static_cast<int>(above);
+    if (cnt == static_cast<uint32_t>(krem) || shift == 0) break;
+  }
+  return Cut{prefix, shift};
+}
+
+// Keep keys[i] (i < n, n <= kKeyCap) with cut.keep(); compacted to the front.
+// Returns the new count (also in *cnt).
+__device__ __forceinline__ uint32_t cta_compact(uint64_t* keys, int n, Cut cut, uint32_t* cnt) {
+  constexpr int kPer = kKeyCap / kThreads;
+  uint64_t reg[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = threadIdx.x + j * kThreads;
+    reg[j] = (i < n) ? keys[i] : 0ull;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *cnt = 0;
+  __syncthreads();
+  int dummy = 0;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = threadIdx.x + j * kThreads;
+    const bool keep = (i < n) && cut.keep(reg[j]);
+    warp_append(keep, reg[j], keys, cnt, kKeyCap, &dummy);
+  }
+  __syncthreads();
+  return *cnt;
+}
+
+// Sort a[0..P) descending; P a power of two.
+__device__ __forceinline__ void cta_bitonic_sort_desc(uint64_t* a, int P) {
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint64_t x = a[i], y = a[ixj];
+          const bool first_half = (i & k) == 0;
+          if (first_half ? (x < y) : (x > y)) {
+            a[i] = y;
+            a[ixj] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// ---------------------------------------------------------------- logit loads
+template <typename TL> struct LogitTraits;
+template <> struct LogitTraits<float> {
+  static constexpr int kPerVec = 4;
+  __device__ static __forceinline__ void unpack(const uint4& v, float* x) {
+    x[0] = __uint_as_float(v.x); x[1] = __uint_as_float(v.y);
+    x[2] = __uint_as_float(v.z); x[3] = __uint_as_float(v.w);
+  }
+  __device__ static __forceinline__ float load1(const float* p) { return __ldg(p); }
+};
+template <> struct LogitTraits<__nv_bfloat16> {
+  static constexpr int kPerVec = 8;
+  __device__ static __forceinline__ void unpack(const uint4& v, float* x) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[2 * i] = __uint_as_float(w[i] << 16);
+      x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  }
+  __device__ static __forceinline__ float load1(const __nv_bfloat16* p) {
+    const unsigned short u = __ldg(reinterpret_cast<const unsigned short*>(p));
+    return __uint_as_float(static_cast<uint32_t>(u) << 16);
+  }
+};
+template <> struct LogitTraits<__half> {
+  static constexpr int kPerVec = 8;
+  __device__ static __forceinline__ void unpack(const uint4& v, float* x) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      float2 f = __half22float2(h);
+      x[2 * i] = f.x;
+      x[2 * i + 1] = f.y;
+    }
+  }
+  __device__ static __forceinline__ float load1(const __half* p) { return __half2float(__ldg(p)); }
+};
+
+}  // namespace gr
