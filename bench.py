@@ -45,7 +45,7 @@ UNIT = "req-steps/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg2", choices=["cfg2", "cfg3", "cfg4"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -165,7 +165,8 @@ def step_kwargs(wl):
 
 
 def algorithmic_bytes(wl, node_np: np.ndarray, hist_len: int) -> int:
-    """Bytes the step must move for R requests ('algorithmic bytes')."""
+    """Algorithmic bytes of one step of R requests: every logit once, CSR rows of the
+    distinct nodes, per-beam inputs and outputs, and the fork table read and write."""
     R, B, V = wl["R"], wl["B"], wl["V"]
     s = 2 if wl["cfg"]["dtype"] == "bf16" else 4
     total = R * B * V * s                       # every logit read once
@@ -241,6 +242,7 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     clocks.start()
+    time.sleep(0.5)          # let nvidia-smi start sampling before the timed region
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
@@ -261,6 +263,7 @@ def run_ours(args):
     # roofline of the fused kernel: algorithmic bytes / device time of each step
     steps_bytes = [bytes_cycle[i % levels] for i in range(args.steps)]
     avg_launch_ms = float(np.mean(per_step_ms))
+    per_level_ms = [round(float(np.mean(per_step_ms[i::levels])), 5) for i in range(min(levels, args.steps))]
     achieved = float(np.mean([b / (ms * 1e-3) for b, ms in zip(steps_bytes, per_step_ms)])) / 1e9
     peak, peak_kind = peaks()
 
@@ -288,7 +291,8 @@ def run_ours(args):
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": None, "kernel": "gr::fused_step_kernel",
                      "algorithmic_bytes_per_launch": int(np.mean(steps_bytes)),
-                     "avg_launch_ms": round(avg_launch_ms, 5)},
+                     "avg_launch_ms": round(avg_launch_ms, 5), "per_level_ms": per_level_ms,
+                     "per_level_bytes": [int(b) for b in bytes_cycle]},
         "gpu_launches": args.steps,
         "clocks": clk,
         "device_errors": err,

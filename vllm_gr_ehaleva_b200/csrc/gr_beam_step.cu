@@ -86,7 +86,8 @@ struct Smem {
   SelectScratch* sel;
   float* red_m;
   float* red_s;
-  uint64_t* bars;
+  uint64_t* full;
+  uint64_t* empty;
   struct Scalars {
     uint32_t cnt;
     uint32_t ntab;
@@ -101,6 +102,8 @@ struct Smem {
     float thr_y;
     uint64_t thr_key;
     uint64_t min_key;
+    long long issued;
+    int producer_done;
   } * v;
 };
 
@@ -117,7 +120,7 @@ __host__ __device__ inline size_t smem_bytes(int stages, int bm_words, int pen) 
   }
   o += align128(sizeof(SelectScratch));
   o += align128(kWarps * 8);
-  o += align128(kMaxStages * 8);
+  o += align128(kMaxStages * 16);
   o += align128(sizeof(Smem::Scalars));
   return o;
 }
@@ -141,7 +144,9 @@ __device__ inline Smem carve(unsigned char* base, const Params& P) {
   S.red_m = reinterpret_cast<float*>(base + o);
   S.red_s = reinterpret_cast<float*>(base + o + kWarps * 4);
   o += align128(kWarps * 8);
-  S.bars = reinterpret_cast<uint64_t*>(base + o); o += align128(kMaxStages * 8);
+  S.full = reinterpret_cast<uint64_t*>(base + o);
+  S.empty = S.full + kMaxStages;
+  o += align128(kMaxStages * 16);
   S.v = reinterpret_cast<Smem::Scalars*>(base + o);
   return S;
 }
@@ -343,24 +348,24 @@ struct Step {
       atomicMax(P.tau + r, static_cast<unsigned long long>(floor_key));
       if (floor_key > S.v->thr_key) S.v->thr_key = floor_key;
     }
-    __syncthreads();
+    csync();
   }
 
   __device__ uint64_t min_key_of_list() {
     const int n = min(static_cast<int>(S.v->cnt), kKeyCap);
     uint64_t mn = ~0ull;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) mn = (S.keys[i] < mn) ? S.keys[i] : mn;
+    for (int i = threadIdx.x; i < n; i += kThreads) mn = (S.keys[i] < mn) ? S.keys[i] : mn;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const uint64_t v = __shfl_xor_sync(0xFFFFFFFFu, mn, o);
       mn = v < mn ? v : mn;
     }
     if (threadIdx.x == 0) S.v->min_key = ~0ull;
-    __syncthreads();
+    csync();
     if (lane_id() == 0) atomicMin(reinterpret_cast<unsigned long long*>(&S.v->min_key), mn);
-    __syncthreads();
+    csync();
     const uint64_t res = S.v->min_key;
-    __syncthreads();
+    csync();
     return res;
   }
 
@@ -370,7 +375,7 @@ struct Step {
     for (int base = c.c0; base < c.c1; base += kBatch) {
       const int end = min(base + kBatch, c.c1);
       const uint64_t thr = S.v->thr_key;
-      for (int jb = base + warp_id() * 32; jb < end; jb += blockDim.x) {
+      for (int jb = base + warp_id() * 32; jb < end; jb += kThreads) {
         const int j = jb + lane;
         bool pred = false;
         uint64_t key = 0;
@@ -395,7 +400,7 @@ struct Step {
         }
         warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
       }
-      __syncthreads();
+      csync();
       if (end < c.c1 && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
         const Cut cut = shrink_to(P.k2);
         raise_tau(c.r, cut.floor_key());
@@ -414,14 +419,14 @@ struct Step {
     if (static_cast<int>(S.v->cnt) > P.kk) {
       shrink_to(P.kk);
       if (threadIdx.x == 0) S.v->discard = 1;
-      __syncthreads();
+      csync();
     }
     const bool discarded = S.v->discard != 0;
     float y_last = -kInf;
     if (discarded) y_last = key_score(min_key_of_list());
     const int n = min(static_cast<int>(S.v->cnt), kKeyCap);
     const uint32_t vb = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = threadIdx.x; i < n; i += kThreads) {
       const uint64_t k = S.keys[i];
       const uint32_t flat = key_flat(k);
       const int tok = static_cast<int>(flat - vb);
@@ -434,7 +439,7 @@ struct Step {
       const float y = exact_y(c, load_logit(c, tl), tl);
       P.eos_score[c.row] = __fadd_rn(c.cum, __fsub_rn(y, lse));
     }
-    __syncthreads();
+    csync();
     if (n > P.k2) shrink_to(P.k2);
     if (discarded && n > 0) {
       const float s_last = __fadd_rn(c.cum, __fsub_rn(y_last, lse));
@@ -449,7 +454,7 @@ struct Step {
     if (static_cast<int>(S.v->cnt) > P.kk) {
       shrink_to(P.kk);
       if (threadIdx.x == 0) S.v->discard = 1;
-      __syncthreads();
+      csync();
     }
     const bool discarded = S.v->discard != 0;
     const uint32_t vb = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V);
@@ -460,14 +465,14 @@ struct Step {
       // every penalised column (value = its penalised logit from the table)
       const int n = min(static_cast<int>(S.v->cnt), kKeyCap);
       uint64_t best = 0;
-      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      for (int i = threadIdx.x; i < n; i += kThreads) {
         const int tl = static_cast<int>(key_flat(S.keys[i]) - vb) - P.voff;
         if (flagged(c, tl)) continue;
         const uint64_t k = make_key(load_logit(c, tl), static_cast<uint32_t>(tl));
         best = k > best ? k : best;
       }
       const int nt = static_cast<int>(S.v->ntab);
-      for (int j = threadIdx.x; j < nt; j += blockDim.x) {
+      for (int j = threadIdx.x; j < nt; j += kThreads) {
         const uint64_t k = make_key(S.tab_xp[j], static_cast<uint32_t>(S.tab_tok[j]));
         best = k > best ? k : best;
       }
@@ -477,21 +482,21 @@ struct Step {
         best = v > best ? v : best;
       }
       if (threadIdx.x == 0) S.v->min_key = 0;
-      __syncthreads();
+      csync();
       if (lane_id() == 0) atomicMax(reinterpret_cast<unsigned long long*>(&S.v->min_key), best);
-      __syncthreads();
+      csync();
       sampled_tl = (S.v->min_key == 0) ? -1 : static_cast<int>(key_flat(S.v->min_key));
-      __syncthreads();
+      csync();
     }
     // value keys -> log-prob keys (ties: lower token first)
     float y_last = -kInf;
     if (discarded) y_last = key_score(min_key_of_list());
     int n = min(static_cast<int>(S.v->cnt), kKeyCap);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = threadIdx.x; i < n; i += kThreads) {
       const uint64_t k = S.keys[i];
       S.keys[i] = make_key(__fsub_rn(key_score(k), lse), key_flat(k));
     }
-    __syncthreads();
+    csync();
     const int K = min(P.K, n);
     if (n > K) shrink_to(K);
     n = min(static_cast<int>(S.v->cnt), kKeyCap);
@@ -503,21 +508,21 @@ struct Step {
     if (sampled_tl >= 0) {
       const uint32_t sflat = vb + static_cast<uint32_t>(P.voff + sampled_tl);
       if (threadIdx.x == 0) S.v->last = 0;
-      __syncthreads();
-      for (int i = threadIdx.x; i < n; i += blockDim.x)
+      csync();
+      for (int i = threadIdx.x; i < n; i += kThreads)
         if (key_flat(S.keys[i]) == sflat) S.v->last = 1;
-      __syncthreads();
+      csync();
       if (S.v->last == 0 && n > 0) {
         // replace the K-th (smallest) entry by the sampled token
         const float ys = exact_y(c, load_logit(c, sampled_tl), sampled_tl);
         const uint64_t sk = make_key(__fsub_rn(ys, lse), sflat);
-        for (int i = threadIdx.x; i < n; i += blockDim.x)
+        for (int i = threadIdx.x; i < n; i += kThreads)
           if (S.keys[i] == kth) S.keys[i] = sk;
       }
-      __syncthreads();
+      csync();
     }
     // catalog mask, cum add, EOS (serving_engine.py:504-506, 511, 541-562)
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = threadIdx.x; i < n; i += kThreads) {
       const uint64_t k = S.keys[i];
       const uint32_t flat = key_flat(k);
       const int tok = static_cast<int>(flat - vb);
@@ -539,7 +544,7 @@ struct Step {
       }
       S.keys[i] = make_key(sc, flat);
     }
-    __syncthreads();
+    csync();
     if (n > P.k2) shrink_to(P.k2);
   }
 
@@ -549,16 +554,16 @@ struct Step {
       const uint64_t t = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
       if (t > S.v->thr_key) S.v->thr_key = t;
     }
-    __syncthreads();
+    csync();
     const uint64_t thr = S.v->thr_key;
     int n = min(static_cast<int>(S.v->cnt), kKeyCap);
     if (thr > 0 && n > 0) n = static_cast<int>(cta_compact(S.keys, n, Cut{thr, 0}, &S.v->cnt));
     if (threadIdx.x == 0) S.v->base = n > 0 ? atomicAdd(P.cnt + c.r, static_cast<unsigned>(n)) : 0u;
-    __syncthreads();
+    csync();
     const long long base = S.v->base;
     if (threadIdx.x == 0 && base + n > P.cap) atomicOr(P.err, GR_DEVERR_OVERFLOW);
     unsigned long long* dst = P.buf + static_cast<size_t>(c.r) * static_cast<size_t>(P.cap);
-    for (int i = threadIdx.x; i < n; i += blockDim.x)
+    for (int i = threadIdx.x; i < n; i += kThreads)
       if (base + i < P.cap) dst[base + i] = S.keys[i];
   }
 
@@ -569,11 +574,11 @@ struct Step {
     if (n > P.cap) n = static_cast<int>(P.cap);
     const int k = min(P.k2, n);
     if (threadIdx.x == 0) S.v->cnt = 0;
-    __syncthreads();
+    csync();
     if (n > k) {
       const Cut cut = cta_radix_select([src](int i) { return __ldcg(src + i); }, n, k, S.sel);
       int dummy = 0;
-      for (int ib = warp_id() * 32; ib < n; ib += blockDim.x) {
+      for (int ib = warp_id() * 32; ib < n; ib += kThreads) {
         const int i = ib + lane_id();
         uint64_t key = 0;
         bool pred = false;
@@ -584,16 +589,16 @@ struct Step {
         warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &dummy);
       }
     } else {
-      for (int i = threadIdx.x; i < n; i += blockDim.x) S.keys[i] = __ldcg(src + i);
+      for (int i = threadIdx.x; i < n; i += kThreads) S.keys[i] = __ldcg(src + i);
     }
-    __syncthreads();
+    csync();
     int P2 = 1;
     while (P2 < k) P2 <<= 1;
-    for (int i = k + threadIdx.x; i < P2; i += blockDim.x) S.keys[i] = 0ull;
-    __syncthreads();
+    for (int i = k + threadIdx.x; i < P2; i += kThreads) S.keys[i] = 0ull;
+    csync();
     cta_bitonic_sort_desc(S.keys, P2);
     const int B = P.B, k2 = P.k2, NB = P.NB, T = P.T;
-    for (int i = threadIdx.x; i < k2; i += blockDim.x) {
+    for (int i = threadIdx.x; i < k2; i += kThreads) {
       float sc = -kInf;
       int tok = -1, par = -1;
       if (i < k) {
@@ -631,7 +636,7 @@ struct Step {
     }
     if (P.hist_out) {
       const int W = T + 1;
-      for (int idx = threadIdx.x; idx < B * W; idx += blockDim.x) {
+      for (int idx = threadIdx.x; idx < B * W; idx += kThreads) {
         const int i = idx / W, t = idx - i * W;
         int v = -1;
         if (i < k) {
@@ -643,12 +648,107 @@ struct Step {
         P.hist_out[static_cast<size_t>(r) * B * W + idx] = v;
       }
     }
-    __syncthreads();
+    csync();
   }
 };
 
+// Add the fast-path accumulators (relative to the same reference max) into s.
+__device__ __forceinline__ void fold(uint64_t& a0, uint64_t& a1, float& s) {
+  float q0, q1, q2, q3;
+  unpack2(a0, q0, q1);
+  unpack2(a1, q2, q3);
+  s += (q0 + q1) + (q2 + q3);
+  a0 = pack2(0.0f, 0.0f);
+  a1 = pack2(0.0f, 0.0f);
+}
+
+// Lazily normalised sum of exp over one chunk share of a thread (fast path):
+// s += sum 2^(x*a - m*log2e) with the running reference m left unchanged unless
+// the partial sum overflows (then the exact per-vector path recomputes it).
 template <typename TL>
-__global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_constant__ Params P) {
+struct FastSum;
+
+template <>
+struct FastSum<__nv_bfloat16> {
+  static constexpr int kWords = 4;   // 32-bit words per 16-byte vector
+  __device__ static __forceinline__ void add(const uint4& v, uint64_t A2, uint64_t C2, uint64_t& p0, uint64_t& p1) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint64_t x2 = pack2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
+      float t0, t1;
+      unpack2(ffma2(x2, A2, C2), t0, t1);
+      const uint64_t e2 = pack2(fast_exp2(t0), fast_exp2(t1));
+      if (i & 1) p1 = fadd2(p1, e2); else p0 = fadd2(p0, e2);
+    }
+  }
+};
+
+template <>
+struct FastSum<__half> {
+  __device__ static __forceinline__ void add(const uint4& v, uint64_t A2, uint64_t C2, uint64_t& p0, uint64_t& p1) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      float t0, t1;
+      unpack2(ffma2(pack2(f.x, f.y), A2, C2), t0, t1);
+      const uint64_t e2 = pack2(fast_exp2(t0), fast_exp2(t1));
+      if (i & 1) p1 = fadd2(p1, e2); else p0 = fadd2(p0, e2);
+    }
+  }
+};
+
+template <>
+struct FastSum<float> {
+  __device__ static __forceinline__ void add(const uint4& v, uint64_t A2, uint64_t C2, uint64_t& p0, uint64_t& p1) {
+    float t0, t1, t2, t3;
+    unpack2(ffma2(pack2(__uint_as_float(v.x), __uint_as_float(v.y)), A2, C2), t0, t1);
+    unpack2(ffma2(pack2(__uint_as_float(v.z), __uint_as_float(v.w)), A2, C2), t2, t3);
+    p0 = fadd2(p0, pack2(fast_exp2(t0), fast_exp2(t1)));
+    p1 = fadd2(p1, pack2(fast_exp2(t2), fast_exp2(t3)));
+  }
+};
+
+// Producer warp, lane 0: fill the ring with the CTA's (row, chunk) sequence.
+template <int ES>
+__device__ void produce(const Params& P, Smem& S, int my_n) {
+  const uint64_t pol = l2_policy_evict_first();
+  int stage = 0;
+  uint32_t round = 0;
+  long long fills = 0;
+  for (int it = 0; it < my_n; ++it) {
+    const Geom g = row_geom<ES>(P, row_of_iter(P, it));
+    for (int ch = 0; ch < g.nchunks; ++ch) {
+      if (fills >= P.stages) {
+        if (!mbar_wait_bounded(&S.empty[stage], (round - 1u) & 1u, &S.v->abort)) {
+          if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
+          S.v->abort = 1;
+          goto done;
+        }
+      }
+      {
+        const long long off = static_cast<long long>(ch) * kStageBytes;
+        const uint32_t bytes = static_cast<uint32_t>(min(static_cast<long long>(kStageBytes), g.body_bytes - off));
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&S.full[stage], bytes);
+        bulk_copy_g2s(S.ring + static_cast<size_t>(stage) * kStageBytes, g.body + off, bytes, &S.full[stage], pol);
+      }
+      ++fills;
+      if (++stage == P.stages) {
+        stage = 0;
+        ++round;
+      }
+    }
+  }
+done:
+  S.v->issued = fills;
+  __threadfence_block();
+  S.v->producer_done = 1;
+}
+
+template <typename TL>
+__global__ void __launch_bounds__(kBlock, 1) fused_step_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Smem S = carve(smem_raw, P);
   Step<TL> st(P, S);
@@ -656,6 +756,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
   constexpr int ES = sizeof(TL);
   constexpr int EPV = Tr::kPerVec;
   constexpr int kChunkElems = kStageBytes / ES;
+  constexpr int kChunkVecs = kStageBytes / 16;
   constexpr int kSubVecs = kBatch / EPV;     // vectors between capacity checks (stream rows)
 
   const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
@@ -663,40 +764,26 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
   const int my_n = (static_cast<int>(blockIdx.x) < total) ? (total - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1 : 0;
 
   if (tid == 0) {
-    for (int s = 0; s < P.stages; ++s) mbar_init(&S.bars[s], 1);
+    for (int s = 0; s < P.stages; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], kWarps);
+    }
     fence_mbar_init();
     S.v->abort = 0;
+    S.v->producer_done = 0;
+    S.v->issued = 0;
   }
   if (P.pen)
-    for (int i = tid; i < P.bm_words; i += blockDim.x) S.bitmap[i] = 0u;
-  __syncthreads();
+    for (int i = tid; i < P.bm_words; i += kBlock) S.bitmap[i] = 0u;
+  __syncthreads();   // the only CTA-wide barrier: consumers use csync() from here on
 
-  // ---- producer state (thread 0 only) ----
-  int p_it = 0, p_c = 0;
-  long long issued = 0;
-  const uint64_t pol = l2_policy_evict_first();
-  auto issue_next = [&]() {
-    while (p_it < my_n) {
-      const Geom g = row_geom<ES>(P, row_of_iter(P, p_it));
-      if (p_c < g.nchunks) {
-        const int stage = static_cast<int>(issued % P.stages);
-        const long long off = static_cast<long long>(p_c) * kStageBytes;
-        const uint32_t bytes = static_cast<uint32_t>(min(static_cast<long long>(kStageBytes), g.body_bytes - off));
-        mbar_arrive_expect_tx(&S.bars[stage], bytes);
-        bulk_copy_g2s(S.ring + static_cast<size_t>(stage) * kStageBytes, g.body + off, bytes, &S.bars[stage], pol);
-        ++issued;
-        ++p_c;
-        return;
-      }
-      ++p_it;
-      p_c = 0;
-    }
-  };
-  if (tid == 0) {
-    fence_proxy_async_smem();
-    for (int s = 0; s < P.stages; ++s) issue_next();
+  if (warp == kWarps) {
+    if (lane == 0) produce<ES>(P, S, my_n);
+    return;
   }
 
+  int cstage = 0;
+  uint32_t cphase = 0;
   long long consumed = 0;
   for (int it = 0; it < my_n; ++it) {
     // ------------------------------------------------------------ row setup
@@ -742,6 +829,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
       c.pen_active = has_pen && (P.mode == kModeProcessed || P.K > 0);
     }
     c.excl = c.pen_active && P.mode == kModeProcessed;
+    const bool fast_ok = !c.stream && !c.excl;
 
     if (tid == 0) {
       S.v->cnt = 0;
@@ -752,10 +840,10 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
       S.v->thr_y = -kInf;
       if (P.eos_score && !P.partial_only) P.eos_score[c.row] = __int_as_float(0x7FC00000);
     }
-    __syncthreads();
+    csync();
     if (c.pen_active) {
       const int* h = P.hist + static_cast<size_t>(c.row) * P.T;
-      for (int t = tid; t < P.T; t += blockDim.x) {
+      for (int t = tid; t < P.T; t += kThreads) {
         const int tok = h[t];
         const int tl = tok - P.voff;
         if (tok >= 0 && tl >= 0 && tl < P.VL) {
@@ -772,19 +860,22 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
           }
         }
       }
-      __syncthreads();
+      csync();
     }
 
     float m = -kInf, s = 0.0f;
     float thr_y = -kInf;
     uint64_t thr_key = 0ull;
     const Geom g = row_geom<ES>(P, c.row);
+    // fast-path scale: exp(y - m) = 2^(x * a - m * log2e) with y = x (raw) or x / T
+    const float a = kLog2e * ((P.mode == kModeProcessed) ? c.rteff : 1.0f);
+    uint64_t sacc0 = pack2(0.0f, 0.0f), sacc1 = pack2(0.0f, 0.0f);
 
     // ------------------------------------------------------- head / tail scalars
     {
       const int nh = g.head, nt = P.VL - g.tail_start;
       const int ns = nh + nt;
-      for (int ib = warp * 32; ib < ns; ib += blockDim.x) {
+      for (int ib = warp * 32; ib < ns; ib += kThreads) {
         const int i = ib + lane;
         const bool valid = i < ns;
         const int tl = valid ? ((i < nh) ? i : g.tail_start + (i - nh)) : 0;
@@ -796,19 +887,58 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
 
     // ------------------------------------------------------------ body chunks
     for (int ch = 0; ch < g.nchunks; ++ch) {
-      const int stage = static_cast<int>(consumed % P.stages);
-      const uint32_t parity = static_cast<uint32_t>((consumed / P.stages) & 1);
-      if (!mbar_wait_bounded(&S.bars[stage], parity)) {
+      if (!mbar_wait_bounded(&S.full[cstage], cphase, &S.v->abort)) {
+        if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
         S.v->abort = 1;
-        atomicOr(P.err, GR_DEVERR_TIMEOUT);
       }
       const long long off = static_cast<long long>(ch) * kStageBytes;
       const int bytes = static_cast<int>(min(static_cast<long long>(kStageBytes), g.body_bytes - off));
       const int nvec = bytes >> 4;
-      const uint4* sv = reinterpret_cast<const uint4*>(S.ring + static_cast<size_t>(stage) * kStageBytes);
+      const uint4* sv = reinterpret_cast<const uint4*>(S.ring + static_cast<size_t>(cstage) * kStageBytes);
       const int tbase = g.head + ch * kChunkElems;
-      if (!c.stream) {
-        for (int vb = warp * 32; vb < nvec; vb += blockDim.x) {
+      const bool in_window = c.constrained && tbase + kChunkElems > c.wlo && tbase <= c.whi;
+      if (fast_ok && !in_window) {
+        // fast path: two 16-byte vectors per thread, packed f32x2 math
+        const bool v0ok = tid < nvec, v1ok = tid + kThreads < nvec;
+        const uint4 v0 = v0ok ? sv[tid] : make_uint4(0, 0, 0, 0);
+        const uint4 v1 = v1ok ? sv[tid + kThreads] : make_uint4(0, 0, 0, 0);
+        static_assert(kChunkVecs == 2 * kThreads, "two vectors per thread per stage");
+        const float cm = -m * kLog2e;
+        const uint64_t A2 = pack2(a, a), C2 = pack2(cm, cm);
+        uint64_t p0 = pack2(0.0f, 0.0f), p1 = pack2(0.0f, 0.0f);
+        if (v0ok) FastSum<TL>::add(v0, A2, C2, p0, p1);
+        if (v1ok) FastSum<TL>::add(v1, A2, C2, p0, p1);
+        float q0, q1, q2, q3;
+        unpack2(p0, q0, q1);
+        unpack2(p1, q2, q3);
+        const float tot = (q0 + q1) + (q2 + q3);
+        if (tot <= 1.0e30f) {
+          sacc0 = fadd2(sacc0, p0);
+          sacc1 = fadd2(sacc1, p1);
+        } else {
+          // first chunk of the row, a large partial sum or non-finite input:
+          // fold the fast accumulators (same reference m) and take the exact path
+          fold(sacc0, sacc1, s);
+          if (v0ok) {
+            float x[EPV];
+            Tr::unpack(v0, x);
+            float y[EPV];
+#pragma unroll
+            for (int i = 0; i < EPV; ++i) y[i] = (P.mode == kModeProcessed) ? x[i] * c.rteff : x[i];
+            st.template lse_update<EPV>(y, m, s);
+          }
+          if (v1ok) {
+            float x[EPV];
+            Tr::unpack(v1, x);
+            float y[EPV];
+#pragma unroll
+            for (int i = 0; i < EPV; ++i) y[i] = (P.mode == kModeProcessed) ? x[i] * c.rteff : x[i];
+            st.template lse_update<EPV>(y, m, s);
+          }
+        }
+      } else if (!c.stream) {
+        fold(sacc0, sacc1, s);
+        for (int vb = warp * 32; vb < nvec; vb += kThreads) {
           const int v = vb + lane;
           const bool valid = v < nvec;
           float x[EPV];
@@ -821,9 +951,10 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
           st.template process<EPV>(c, x, tbase + v * EPV, valid, m, s, thr_y, thr_key);
         }
       } else {
+        fold(sacc0, sacc1, s);
         for (int sb = 0; sb < nvec; sb += kSubVecs) {
           const int send = min(nvec, sb + kSubVecs);
-          for (int vb = sb + warp * 32; vb < send; vb += blockDim.x) {
+          for (int vb = sb + warp * 32; vb < send; vb += kThreads) {
             const int v = vb + lane;
             const bool valid = v < send;
             float x[EPV];
@@ -835,7 +966,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
             }
             st.template process<EPV>(c, x, tbase + v * EPV, valid, m, s, thr_y, thr_key);
           }
-          __syncthreads();
+          csync();
           if (static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
             const Cut cut = st.shrink_to(P.kk);
             if (tid == 0) {
@@ -844,26 +975,28 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
               const float ty = key_score(cut.floor_key());
               S.v->thr_y = ty - fabsf(ty) * 2.0e-6f - 1e-30f;
             }
-            __syncthreads();
+            csync();
             thr_key = S.v->thr_key;
             thr_y = S.v->thr_y;
           }
         }
       }
-      __syncthreads();
-      if (S.v->abort) goto drain;
-      if (tid == 0) {
-        fence_proxy_async_smem();
-        issue_next();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.empty[cstage]);
+      if (++cstage == P.stages) {
+        cstage = 0;
+        cphase ^= 1u;
       }
       ++consumed;
     }
+
+    fold(sacc0, sacc1, s);
 
     // ------------------------------------------------------------ row end
     if (c.excl) {
       // penalised tokens were left out of the stream; add their exact values
       const int nt = static_cast<int>(S.v->ntab);
-      for (int jb = warp * 32; jb < nt; jb += blockDim.x) {
+      for (int jb = warp * 32; jb < nt; jb += kThreads) {
         const int j = jb + lane;
         const bool valid = j < nt;
         float y[1];
@@ -881,7 +1014,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
         }
       }
     }
-    // CTA reduction of (m, s)
+    // consumer-wide reduction of (m, s)
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float m2 = __shfl_xor_sync(0xFFFFFFFFu, m, o);
@@ -898,7 +1031,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
       S.red_m[warp] = m;
       S.red_s[warp] = s;
     }
-    __syncthreads();
+    csync();
     if (tid == 0) {
       float M = -kInf;
       for (int w = 0; w < kWarps; ++w) M = fmaxf(M, S.red_m[w]);
@@ -911,13 +1044,14 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
       if (P.lse_out) P.lse_out[c.row] = S.v->lse;
       if (P.partial_only) P.partials[c.row] = make_float2(M, tot);
     }
-    __syncthreads();
+    csync();
+    if (S.v->abort) goto drain;
     const float lse = S.v->lse;
 
     if (!P.partial_only) {
       if (c.constrained) {
         if (tid == 0) S.v->thr_key = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
-        __syncthreads();
+        csync();
         st.constrained_candidates(c, lse);
       } else if (c.stream && P.K == 0) {
         st.unconstrained_candidates(c, lse);
@@ -928,16 +1062,16 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
       if (c.stream) {
         // the row-local threshold was over value keys; only the request bound applies now
         if (tid == 0) S.v->thr_key = 0ull;
-        __syncthreads();
+        csync();
       }
       st.emit(c);
       __threadfence();
-      __syncthreads();
+      csync();
       if (tid == 0) {
         const unsigned prev = atomicAdd(P.done + c.r, 1u);
         S.v->last = (prev == static_cast<unsigned>(P.NB - 1)) ? 1 : 0;
       }
-      __syncthreads();
+      csync();
       if (S.v->last) {
         __threadfence();
         st.merge_request(c.r);
@@ -945,22 +1079,30 @@ __global__ void __launch_bounds__(kThreads, 1) fused_step_kernel(const __grid_co
     }
     if (c.pen_active) {
       const int nt = static_cast<int>(S.v->ntab);
-      for (int j = tid; j < nt; j += blockDim.x) S.bitmap[S.tab_tok[j] >> 5] = 0u;
+      for (int j = tid; j < nt; j += kThreads) S.bitmap[S.tab_tok[j] >> 5] = 0u;
     }
-    __syncthreads();
+    csync();
   }
   return;
 
 drain:
-  // A bounded wait ran out: wait (bounded) for this CTA's copies still in
-  // flight so that none lands after the CTA has exited, then leave.
+  // A bounded wait ran out: wait (bounded) for the producer to stop and for
+  // the copies it issued that were not consumed, so that none lands after the
+  // CTA has exited.
   if (tid == 0) {
+    const uint64_t t0 = global_timer_ns();
+    while (!*reinterpret_cast<volatile int*>(&S.v->producer_done) && global_timer_ns() - t0 < kWaitLimitNs) {
+    }
+    const long long issued = *reinterpret_cast<volatile long long*>(&S.v->issued);
     for (long long q = consumed; q < issued; ++q) {
-      const int stage = static_cast<int>(q % P.stages);
-      mbar_wait_bounded(&S.bars[stage], static_cast<uint32_t>((q / P.stages) & 1));
+      mbar_wait_bounded(&S.full[cstage], cphase);
+      if (++cstage == P.stages) {
+        cstage = 0;
+        cphase ^= 1u;
+      }
     }
   }
-  __syncthreads();
+  csync();
 }
 
 // ============================================================== host side
@@ -1077,7 +1219,7 @@ static int launch_fused(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream_t 
   }
   const int total = P.R * P.NB;
   const int grid = total < dev->sms ? total : dev->sms;
-  fused_step_kernel<TL><<<grid, kThreads, smem, stream>>>(P);
+  fused_step_kernel<TL><<<grid, kBlock, smem, stream>>>(P);
   if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
   return GR_OK;
 }

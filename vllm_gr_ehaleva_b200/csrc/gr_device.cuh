@@ -15,7 +15,8 @@
 
 namespace gr {
 
-constexpr int kThreads = 512;                 // one CTA per SM, persistent
+constexpr int kThreads = 512;                 // consumer threads (one CTA per SM, persistent)
+constexpr int kBlock = kThreads + 32;         // + one producer warp
 constexpr int kWarps = kThreads / 32;
 constexpr int kStageBytes = 16384;            // one TMA bulk copy per stage
 constexpr int kMaxStages = 8;
@@ -31,6 +32,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 #define kInf (__int_as_float(0x7f800000))
 
 // ---------------------------------------------------------------- PTX helpers
+// Barrier among the kThreads consumer threads only (named barrier 1); the
+// producer warp never takes part, so it can keep prefetching meanwhile.
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -52,6 +57,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -70,12 +79,15 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
-// Wait for the phase with the given parity to complete; false after kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+// Wait for the phase with the given parity to complete.  Gives up (false)
+// after kWaitLimitNs, or as soon as *abort is set when abort is non-null.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  const volatile int* abort = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (abort != nullptr && *abort) return false;
     if (global_timer_ns() - t0 > kWaitLimitNs) return false;
   }
 }
@@ -102,6 +114,26 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed float2 arithmetic (sm_100: one instruction for two lanes of f32).
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
 }
 
 // ---------------------------------------------------------------- keys
@@ -175,10 +207,10 @@ __device__ Cut cta_radix_select(KeyFn keyf, int n, int k, SelectScratch* sc) {
   const int lane = lane_id();
   while (true) {
     shift -= 8;
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) sc->hist[i] = 0;
-    __syncthreads();
+    for (int i = threadIdx.x; i < 256; i += kThreads) sc->hist[i] = 0;
+    csync();
     const int hs = shift + 8;
-    for (int ib = warp_id() * 32; ib < n; ib += blockDim.x) {
+    for (int ib = warp_id() * 32; ib < n; ib += kThreads) {
       const int i = ib + lane;
       uint32_t digit = 256u;
       if (i < n) {
@@ -189,7 +221,7 @@ __device__ Cut cta_radix_select(KeyFn keyf, int n, int k, SelectScratch* sc) {
       const unsigned peers = __match_any_sync(0xFFFFFFFFu, digit);
       if (digit < 256u && lane == __ffs(peers) - 1) atomicAdd(&sc->hist[digit], static_cast<uint32_t>(__popc(peers)));
     }
-    __syncthreads();
+    csync();
     if (warp_id() == 0) {
       uint32_t c[8];
       uint32_t sum = 0;
@@ -219,9 +251,9 @@ __device__ Cut cta_radix_select(KeyFn keyf, int n, int k, SelectScratch* sc) {
         }
       }
     }
-    __syncthreads();
+    csync();
     const uint32_t d = sc->digit, above = sc->above, cnt = sc->count;
-    __syncthreads();
+    csync();
     prefix |= static_cast<uint64_t>(d) << shift;
     krem -= static_cast<int>(above);
     if (cnt == static_cast<uint32_t>(krem) || shift == 0) break;
@@ -239,9 +271,9 @@ __device__ __forceinline__ uint32_t cta_compact(uint64_t* keys, int n, Cut cut, 
     const int i = threadIdx.x + j * kThreads;
     reg[j] = (i < n) ? keys[i] : 0ull;
   }
-  __syncthreads();
+  csync();
   if (threadIdx.x == 0) *cnt = 0;
-  __syncthreads();
+  csync();
   int dummy = 0;
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
@@ -249,7 +281,7 @@ __device__ __forceinline__ uint32_t cta_compact(uint64_t* keys, int n, Cut cut, 
     const bool keep = (i < n) && cut.keep(reg[j]);
     warp_append(keep, reg[j], keys, cnt, kKeyCap, &dummy);
   }
-  __syncthreads();
+  csync();
   return *cnt;
 }
 
@@ -257,7 +289,7 @@ __device__ __forceinline__ uint32_t cta_compact(uint64_t* keys, int n, Cut cut, 
 __device__ __forceinline__ void cta_bitonic_sort_desc(uint64_t* a, int P) {
   for (int k = 2; k <= P; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+      for (int i = threadIdx.x; i < P; i += kThreads) {
         const int ixj = i ^ j;
         if (ixj > i) {
           const uint64_t x = a[i], y = a[ixj];
@@ -268,7 +300,7 @@ __device__ __forceinline__ void cta_bitonic_sort_desc(uint64_t* a, int P) {
           }
         }
       }
-      __syncthreads();
+      csync();
     }
   }
 }
