@@ -21,6 +21,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cuda_runtime.h>
+#include <type_traits>
 
 #include "../../include/gr_beam.h"
 #include "gr_device.cuh"
@@ -78,7 +79,7 @@ struct Params {
 struct Smem {
   unsigned char* ring;
   uint64_t* keys;
-  float* win;
+  unsigned char* win;   // raw logits of the child window
   uint32_t* bitmap;
   int* tab_tok;
   float* tab_xp;
@@ -102,6 +103,7 @@ struct Smem {
     float thr_y;
     uint64_t thr_key;
     uint64_t min_key;
+    uint64_t tau_pref;
     long long issued;
     int producer_done;
   } * v;
@@ -113,7 +115,7 @@ __host__ __device__ inline size_t smem_bytes(int stages, int bm_words, int pen) 
   size_t o = 0;
   o += align128(size_t(stages) * kStageBytes);
   o += align128(size_t(kKeyCap) * 8);
-  o += align128(size_t(kWin) * 4);
+  o += align128(size_t(kWinBytes));
   if (pen) {
     o += align128(size_t(bm_words) * 4);
     o += align128(size_t(kPenTableMax) * 12);
@@ -130,7 +132,7 @@ __device__ inline Smem carve(unsigned char* base, const Params& P) {
   size_t o = 0;
   S.ring = base + o; o += align128(size_t(P.stages) * kStageBytes);
   S.keys = reinterpret_cast<uint64_t*>(base + o); o += align128(size_t(kKeyCap) * 8);
-  S.win = reinterpret_cast<float*>(base + o); o += align128(size_t(kWin) * 4);
+  S.win = base + o; o += align128(size_t(kWinBytes));
   if (P.pen) {
     S.bitmap = reinterpret_cast<uint32_t*>(base + o); o += align128(size_t(P.bm_words) * 4);
     S.tab_tok = reinterpret_cast<int*>(base + o);
@@ -240,6 +242,27 @@ struct Step {
     return Tr::load1(rowp + tl);
   }
 
+  static constexpr int kWinTok = kWinBytes / ES;
+
+  __device__ __forceinline__ void win_store(int i, float x) const {
+    if constexpr (ES == 4) {
+      reinterpret_cast<float*>(S.win)[i] = x;
+    } else if constexpr (std::is_same_v<TL, __nv_bfloat16>) {
+      reinterpret_cast<unsigned short*>(S.win)[i] = static_cast<unsigned short>(__float_as_uint(x) >> 16);
+    } else {
+      reinterpret_cast<__half*>(S.win)[i] = __float2half_rn(x);
+    }
+  }
+  __device__ __forceinline__ float win_load(int i) const {
+    if constexpr (ES == 4) {
+      return reinterpret_cast<const float*>(S.win)[i];
+    } else if constexpr (std::is_same_v<TL, __nv_bfloat16>) {
+      return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const unsigned short*>(S.win)[i]) << 16);
+    } else {
+      return __half2float(reinterpret_cast<const __half*>(S.win)[i]);
+    }
+  }
+
   __device__ __forceinline__ bool flagged(const RowCtx& c, int tl) const {
     return c.pen_active && ((S.bitmap[tl >> 5] >> (tl & 31)) & 1u);
   }
@@ -307,7 +330,7 @@ struct Step {
 #pragma unroll
         for (int i = 0; i < N; ++i) {
           const int tl = tb + i;
-          if (tl >= c.wlo && tl <= c.whi) S.win[tl - c.wlo] = x[i];
+          if (tl >= c.wlo && tl <= c.whi) win_store(tl - c.wlo, x[i]);
         }
       }
     }
@@ -371,22 +394,31 @@ struct Step {
 
   // ---- row-end candidate formation -----------------------------------------
   __device__ void constrained_candidates(const RowCtx& c, float lse) {
-    const int lane = lane_id();
+    constexpr int kPer = kBatch / kThreads;
     for (int base = c.c0; base < c.c1; base += kBatch) {
       const int end = min(base + kBatch, c.c1);
       const uint64_t thr = S.v->thr_key;
-      for (int jb = base + warp_id() * 32; jb < end; jb += kThreads) {
-        const int j = jb + lane;
+      // issue every child-token load of the batch before using any of them
+      int toks[kPer];
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int j = base + i * kThreads + static_cast<int>(threadIdx.x);
+        toks[i] = (j < end) ? __ldg(P.child_tok + j) : -1;
+      }
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        if (base + i * kThreads >= end) break;           // uniform across the CTA
+        const int j = base + i * kThreads + static_cast<int>(threadIdx.x);
         bool pred = false;
         uint64_t key = 0;
         if (j < end) {
-          const int tok = P.child_tok[j];
+          const int tok = toks[i];
           if (tok < 0 || tok >= P.V) {
             atomicOr(P.err, GR_DEVERR_BAD_CHILD);
           } else {
             const int tl = tok - P.voff;
             if (tl >= 0 && tl < P.VL) {
-              const float x = (tl >= c.wlo && tl <= c.whi) ? S.win[tl - c.wlo] : load_logit(c, tl);
+              const float x = (tl >= c.wlo && tl <= c.whi) ? win_load(tl - c.wlo) : load_logit(c, tl);
               const float y = exact_y(c, x, tl);
               float sc = __fadd_rn(c.cum, __fsub_rn(y, lse));
               if (tok == P.eos) {
@@ -551,7 +583,7 @@ struct Step {
   // Append the row's keys that beat the request threshold; returns nothing.
   __device__ void emit(const RowCtx& c) {
     if (threadIdx.x == 0) {
-      const uint64_t t = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
+      const uint64_t t = S.v->tau_pref;       // read at row start; a stale bound is still valid
       if (t > S.v->thr_key) S.v->thr_key = t;
     }
     csync();
@@ -748,7 +780,7 @@ done:
 }
 
 template <typename TL>
-__global__ void __launch_bounds__(kBlock, 1) fused_step_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Smem S = carve(smem_raw, P);
   Step<TL> st(P, S);
@@ -810,7 +842,7 @@ __global__ void __launch_bounds__(kBlock, 1) fused_step_kernel(const __grid_cons
       const int hi = min(P.child_tok[c.c1 - 1] - P.voff, P.VL - 1);
       if (lo <= hi) {
         c.wlo = lo;
-        c.whi = min(hi, lo + kWin - 1);
+        c.whi = min(hi, lo + Step<TL>::kWinTok - 1);
       }
     }
     c.cum = P.cum[c.row];
@@ -863,6 +895,10 @@ __global__ void __launch_bounds__(kBlock, 1) fused_step_kernel(const __grid_cons
       csync();
     }
 
+    // the request's running threshold: loaded now, used after the stream
+    uint64_t tau_pref = 0;
+    if (tid == 0 && !P.partial_only) tau_pref = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
+
     float m = -kInf, s = 0.0f;
     float thr_y = -kInf;
     uint64_t thr_key = 0ull;
@@ -898,16 +934,19 @@ __global__ void __launch_bounds__(kBlock, 1) fused_step_kernel(const __grid_cons
       const int tbase = g.head + ch * kChunkElems;
       const bool in_window = c.constrained && tbase + kChunkElems > c.wlo && tbase <= c.whi;
       if (fast_ok && !in_window) {
-        // fast path: two 16-byte vectors per thread, packed f32x2 math
-        const bool v0ok = tid < nvec, v1ok = tid + kThreads < nvec;
-        const uint4 v0 = v0ok ? sv[tid] : make_uint4(0, 0, 0, 0);
-        const uint4 v1 = v1ok ? sv[tid + kThreads] : make_uint4(0, 0, 0, 0);
-        static_assert(kChunkVecs == 2 * kThreads, "two vectors per thread per stage");
+        // fast path: kVecPerThread 16-byte vectors per thread, packed f32x2 math
+        constexpr int kVecPerThread = kChunkVecs / kThreads;
+        static_assert(kChunkVecs % kThreads == 0, "whole vectors per thread per stage");
+        uint4 vv[kVecPerThread];
+#pragma unroll
+        for (int j = 0; j < kVecPerThread; ++j)
+          vv[j] = (tid + j * kThreads < nvec) ? sv[tid + j * kThreads] : make_uint4(0, 0, 0, 0);
         const float cm = -m * kLog2e;
         const uint64_t A2 = pack2(a, a), C2 = pack2(cm, cm);
         uint64_t p0 = pack2(0.0f, 0.0f), p1 = pack2(0.0f, 0.0f);
-        if (v0ok) FastSum<TL>::add(v0, A2, C2, p0, p1);
-        if (v1ok) FastSum<TL>::add(v1, A2, C2, p0, p1);
+#pragma unroll
+        for (int j = 0; j < kVecPerThread; ++j)
+          if (tid + j * kThreads < nvec) FastSum<TL>::add(vv[j], A2, C2, p0, p1);
         float q0, q1, q2, q3;
         unpack2(p0, q0, q1);
         unpack2(p1, q2, q3);
@@ -919,21 +958,16 @@ __global__ void __launch_bounds__(kBlock, 1) fused_step_kernel(const __grid_cons
           // first chunk of the row, a large partial sum or non-finite input:
           // fold the fast accumulators (same reference m) and take the exact path
           fold(sacc0, sacc1, s);
-          if (v0ok) {
-            float x[EPV];
-            Tr::unpack(v0, x);
-            float y[EPV];
 #pragma unroll
-            for (int i = 0; i < EPV; ++i) y[i] = (P.mode == kModeProcessed) ? x[i] * c.rteff : x[i];
-            st.template lse_update<EPV>(y, m, s);
-          }
-          if (v1ok) {
-            float x[EPV];
-            Tr::unpack(v1, x);
-            float y[EPV];
+          for (int j = 0; j < kVecPerThread; ++j) {
+            if (tid + j * kThreads < nvec) {
+              float x[EPV];
+              Tr::unpack(vv[j], x);
+              float y[EPV];
 #pragma unroll
-            for (int i = 0; i < EPV; ++i) y[i] = (P.mode == kModeProcessed) ? x[i] * c.rteff : x[i];
-            st.template lse_update<EPV>(y, m, s);
+              for (int i = 0; i < EPV; ++i) y[i] = (P.mode == kModeProcessed) ? x[i] * c.rteff : x[i];
+              st.template lse_update<EPV>(y, m, s);
+            }
           }
         }
       } else if (!c.stream) {
@@ -1049,8 +1083,9 @@ __global__ void __launch_bounds__(kBlock, 1) fused_step_kernel(const __grid_cons
     const float lse = S.v->lse;
 
     if (!P.partial_only) {
+      if (tid == 0) S.v->tau_pref = tau_pref;
       if (c.constrained) {
-        if (tid == 0) S.v->thr_key = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
+        if (tid == 0) S.v->thr_key = tau_pref;
         csync();
         st.constrained_candidates(c, lse);
       } else if (c.stream && P.K == 0) {
@@ -1109,6 +1144,8 @@ drain:
 struct DeviceInfo {
   int sms = 0;
   int smem_optin = 0;
+  int smem_per_sm = 0;
+  int smem_reserved = 0;
   int major = 0;
   bool attr_set[3] = {false, false, false};
 };
@@ -1125,6 +1162,13 @@ static int device_info(DeviceInfo** out) {
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return GR_ERR_CUDA;
     if (cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return GR_ERR_CUDA;
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return GR_ERR_CUDA;
+    int per_sm = 0, reserved = 0;
+    if (cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess)
+      return GR_ERR_CUDA;
+    if (cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess)
+      return GR_ERR_CUDA;
+    d.smem_per_sm = per_sm;
+    d.smem_reserved = reserved;
     d.smem_optin = smem;
     d.major = major;
     d.sms = sms;
@@ -1203,22 +1247,50 @@ static void fill_params(Params& P, const gr_step_desc* d, const gr_step_io* io) 
   P.partials = nullptr;
 }
 
+// Two CTAs per SM when at least three ring stages fit beside the fixed
+// shared-memory pieces (one CTA's row-end work then overlaps the other CTA's
+// streaming); otherwise one CTA per SM with as many stages as fit.
+static int pick_stages(const Params& P, const DeviceInfo* dev, int* ctas_per_sm) {
+  const size_t optin = static_cast<size_t>(dev->smem_optin);
+  const size_t per_sm = static_cast<size_t>(dev->smem_per_sm);
+  const size_t rsv = static_cast<size_t>(dev->smem_reserved);
+  for (int st = kMaxStages; st >= 3; --st) {
+    const size_t b = smem_bytes(st, P.bm_words, P.pen);
+    if (b <= optin && 2 * (b + rsv) <= per_sm) {
+      *ctas_per_sm = 2;
+      return st;
+    }
+  }
+  for (int st = kMaxStages; st >= 2; --st) {
+    if (smem_bytes(st, P.bm_words, P.pen) <= optin) {
+      *ctas_per_sm = 1;
+      return st;
+    }
+  }
+  return 0;
+}
+
 template <typename TL>
 static int launch_fused(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream_t stream) {
-  // as many ring stages as fit beside the fixed pieces
-  int stages = kMaxStages;
-  while (stages > 2 && smem_bytes(stages, P.bm_words, P.pen) > static_cast<size_t>(dev->smem_optin)) --stages;
-  const size_t smem = smem_bytes(stages, P.bm_words, P.pen);
-  if (smem > static_cast<size_t>(dev->smem_optin)) return GR_ERR_UNSUPPORTED;
+  int per = 1;
+  const int stages = pick_stages(P, dev, &per);
+  if (stages == 0) return GR_ERR_UNSUPPORTED;
   P.stages = stages;
+  const size_t smem = smem_bytes(stages, P.bm_words, P.pen);
   if (!dev->attr_set[dtype_idx]) {
     if (cudaFuncSetAttribute(fused_step_kernel<TL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              dev->smem_optin) != cudaSuccess)
       return GR_ERR_CUDA;
     dev->attr_set[dtype_idx] = true;
   }
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fused_step_kernel<TL>, kBlock, smem) != cudaSuccess)
+    return GR_ERR_CUDA;
+  if (occ < 1) return GR_ERR_UNSUPPORTED;
+  if (occ < per) per = occ;
   const int total = P.R * P.NB;
-  const int grid = total < dev->sms ? total : dev->sms;
+  const int slots = dev->sms * per;
+  const int grid = total < slots ? total : slots;
   fused_step_kernel<TL><<<grid, kBlock, smem, stream>>>(P);
   if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
   return GR_OK;

@@ -15,14 +15,14 @@
 
 namespace gr {
 
-constexpr int kThreads = 512;                 // consumer threads (one CTA per SM, persistent)
+constexpr int kThreads = 256;                 // consumer threads per CTA (two CTAs per SM)
 constexpr int kBlock = kThreads + 32;         // + one producer warp
 constexpr int kWarps = kThreads / 32;
 constexpr int kStageBytes = 16384;            // one TMA bulk copy per stage
 constexpr int kMaxStages = 8;
-constexpr int kWin = 8192;                    // child-window tokens kept per row
-constexpr int kKeyCap = 8192;                 // candidate keys in shared memory
-constexpr int kBatch = 4096;                  // max insertions between capacity checks
+constexpr int kWinBytes = 16384;              // child window, raw logits of the row
+constexpr int kKeyCap = 4096;                 // candidate keys in shared memory
+constexpr int kBatch = 2048;                  // max insertions between capacity checks
 constexpr int kPenTableMax = 1024;            // max history tokens with penalties
 constexpr int kSlack = 64;                    // extra keys kept by streamed top-k
 constexpr int kMaxBitmapWords = 8192;         // penalties: local vocab <= 262144
