@@ -30,6 +30,22 @@ namespace gr {
 
 constexpr int kModeProcessed = 1;
 
+// Optional per-phase cycle counters (compile with -DGR_PHASE_PROFILE; off in
+// the product build).  Thread 0 of every CTA adds clock64 deltas per phase.
+#ifdef GR_PHASE_PROFILE
+constexpr int kProfSlots = 16;
+__device__ unsigned long long g_phase[1024][kProfSlots];
+#define GR_PROF_T(var) const long long var = clock64()
+#define GR_PROF_ADD(slot, t0) \
+  do { if (threadIdx.x == 0) g_phase[blockIdx.x][slot] += clock64() - (t0); } while (0)
+#define GR_PROF_CNT(slot) \
+  do { if (threadIdx.x == 0) g_phase[blockIdx.x][slot] += 1; } while (0)
+#else
+#define GR_PROF_T(var)
+#define GR_PROF_ADD(slot, t0) do { } while (0)
+#define GR_PROF_CNT(slot) do { } while (0)
+#endif
+
 struct Params {
   // descriptor
   int R, NB, B, V, VL, voff;
@@ -61,10 +77,8 @@ struct Params {
   int* err;
   // workspace
   unsigned long long* tau;     // [R] running lower bound of the request's 2B-th key
-  unsigned int* cnt;           // [R] keys appended
-  unsigned int* done;          // [R] rows finished
-  unsigned long long* buf;     // [R][cap]
-  long long cap;
+  unsigned int* rowcnt;        // [R*NB] keys in each row's slot
+  unsigned long long* buf;     // [R*NB][2B] per-row candidate slots
   // derived
   int k2;        // 2B candidates
   int kk;        // streamed keep count: max(2B, K) + slack
@@ -75,7 +89,48 @@ struct Params {
   float2* partials;
 };
 
-// Shared-memory carve-up (dynamic shared memory, 128-byte aligned pieces).
+// Shared-memory layout (dynamic shared memory).  Every piece but the ring sits
+// at a compile-time offset, so accesses need no pointer arithmetic at run time;
+// the optional penalty pieces follow, and the ring of bulk-copy stages is last.
+struct Scalars {
+  uint32_t cnt;
+  uint32_t ntab;
+  int overflow;
+  int abort;
+  int last;
+  int discard;
+  uint32_t base;
+  float lse;
+  float m_tot;
+  float s_tot;
+  float thr_y;
+  uint64_t thr_key;
+  uint64_t min_key;
+  uint64_t tau_pref;
+  long long issued;
+  int producer_done;
+};
+
+__host__ __device__ constexpr size_t align128(size_t x) { return (x + 127) & ~size_t(127); }
+
+constexpr size_t kOffKeys = 0;
+constexpr size_t kOffWin = kOffKeys + align128(size_t(kKeyCap) * 8);
+constexpr size_t kOffSel = kOffWin + align128(size_t(kWinBytes));
+constexpr size_t kOffRed = kOffSel + align128(sizeof(SelectScratch));
+constexpr size_t kOffBars = kOffRed + align128(kWarps * 8);
+constexpr size_t kOffScal = kOffBars + align128(kMaxStages * 16);
+constexpr size_t kOffVar = kOffScal + align128(sizeof(Scalars));
+
+__host__ __device__ inline size_t pen_bytes(int bm_words, int pen) {
+  return pen ? align128(size_t(bm_words) * 4) + align128(size_t(kPenTableMax) * 12) : 0;
+}
+
+__host__ __device__ inline size_t smem_bytes(int stages, int bm_words, int pen) {
+  return kOffVar + pen_bytes(bm_words, pen) + align128(size_t(stages) * kStageBytes);
+}
+
+extern __shared__ __align__(128) unsigned char g_smem[];
+
 struct Smem {
   unsigned char* ring;
   uint64_t* keys;
@@ -89,67 +144,26 @@ struct Smem {
   float* red_s;
   uint64_t* full;
   uint64_t* empty;
-  struct Scalars {
-    uint32_t cnt;
-    uint32_t ntab;
-    int overflow;
-    int abort;
-    int last;
-    int discard;
-    uint32_t base;
-    float lse;
-    float m_tot;
-    float s_tot;
-    float thr_y;
-    uint64_t thr_key;
-    uint64_t min_key;
-    uint64_t tau_pref;
-    long long issued;
-    int producer_done;
-  } * v;
+  Scalars* v;
 };
 
-__host__ __device__ inline size_t align128(size_t x) { return (x + 127) & ~size_t(127); }
-
-__host__ __device__ inline size_t smem_bytes(int stages, int bm_words, int pen) {
-  size_t o = 0;
-  o += align128(size_t(stages) * kStageBytes);
-  o += align128(size_t(kKeyCap) * 8);
-  o += align128(size_t(kWinBytes));
-  if (pen) {
-    o += align128(size_t(bm_words) * 4);
-    o += align128(size_t(kPenTableMax) * 12);
-  }
-  o += align128(sizeof(SelectScratch));
-  o += align128(kWarps * 8);
-  o += align128(kMaxStages * 16);
-  o += align128(sizeof(Smem::Scalars));
-  return o;
-}
-
-__device__ inline Smem carve(unsigned char* base, const Params& P) {
+// By-value view of the layout; build it inside each function that needs it.
+__device__ __forceinline__ Smem smem_view(const Params& P) {
   Smem S;
-  size_t o = 0;
-  S.ring = base + o; o += align128(size_t(P.stages) * kStageBytes);
-  S.keys = reinterpret_cast<uint64_t*>(base + o); o += align128(size_t(kKeyCap) * 8);
-  S.win = base + o; o += align128(size_t(kWinBytes));
-  if (P.pen) {
-    S.bitmap = reinterpret_cast<uint32_t*>(base + o); o += align128(size_t(P.bm_words) * 4);
-    S.tab_tok = reinterpret_cast<int*>(base + o);
-    S.tab_xp = reinterpret_cast<float*>(base + o + kPenTableMax * 4);
-    S.tab_y = reinterpret_cast<float*>(base + o + kPenTableMax * 8);
-    o += align128(size_t(kPenTableMax) * 12);
-  } else {
-    S.bitmap = nullptr; S.tab_tok = nullptr; S.tab_xp = nullptr; S.tab_y = nullptr;
-  }
-  S.sel = reinterpret_cast<SelectScratch*>(base + o); o += align128(sizeof(SelectScratch));
-  S.red_m = reinterpret_cast<float*>(base + o);
-  S.red_s = reinterpret_cast<float*>(base + o + kWarps * 4);
-  o += align128(kWarps * 8);
-  S.full = reinterpret_cast<uint64_t*>(base + o);
+  S.keys = reinterpret_cast<uint64_t*>(g_smem + kOffKeys);
+  S.win = g_smem + kOffWin;
+  S.sel = reinterpret_cast<SelectScratch*>(g_smem + kOffSel);
+  S.red_m = reinterpret_cast<float*>(g_smem + kOffRed);
+  S.red_s = reinterpret_cast<float*>(g_smem + kOffRed + kWarps * 4);
+  S.full = reinterpret_cast<uint64_t*>(g_smem + kOffBars);
   S.empty = S.full + kMaxStages;
-  o += align128(kMaxStages * 16);
-  S.v = reinterpret_cast<Smem::Scalars*>(base + o);
+  S.v = reinterpret_cast<Scalars*>(g_smem + kOffScal);
+  S.bitmap = reinterpret_cast<uint32_t*>(g_smem + kOffVar);
+  const size_t tab = kOffVar + align128(size_t(P.bm_words) * 4);
+  S.tab_tok = reinterpret_cast<int*>(g_smem + tab);
+  S.tab_xp = reinterpret_cast<float*>(g_smem + tab + kPenTableMax * 4);
+  S.tab_y = reinterpret_cast<float*>(g_smem + tab + kPenTableMax * 8);
+  S.ring = g_smem + kOffVar + pen_bytes(P.bm_words, P.pen);
   return S;
 }
 
@@ -216,6 +230,8 @@ __device__ __forceinline__ float penalise(float x, int cnt, float rep, float pre
 struct RowCtx {
   int row, r, b, node;
   int c0, c1;          // CSR edge range of the node (c0 == c1: none)
+  int lo_tok;          // first child token
+  bool dense;          // children are exactly the tokens lo_tok .. lo_tok + (c1 - c0) - 1
   int wlo, whi;        // window [wlo, whi] in local columns (empty if wlo > whi)
   bool stream;         // unconstrained or reference-literal
   bool constrained;
@@ -233,8 +249,7 @@ struct Step {
   static constexpr int EPV = Tr::kPerVec;
 
   const Params& P;
-  Smem& S;
-  __device__ Step(const Params& p, Smem& s) : P(p), S(s) {}
+  __device__ __forceinline__ explicit Step(const Params& p) : P(p) {}
 
   __device__ __forceinline__ float load_logit(const RowCtx& c, int tl) const {
     const TL* rowp = reinterpret_cast<const TL*>(static_cast<const char*>(P.logits) +
@@ -245,6 +260,7 @@ struct Step {
   static constexpr int kWinTok = kWinBytes / ES;
 
   __device__ __forceinline__ void win_store(int i, float x) const {
+    const Smem S = smem_view(P);
     if constexpr (ES == 4) {
       reinterpret_cast<float*>(S.win)[i] = x;
     } else if constexpr (std::is_same_v<TL, __nv_bfloat16>) {
@@ -254,6 +270,7 @@ struct Step {
     }
   }
   __device__ __forceinline__ float win_load(int i) const {
+    const Smem S = smem_view(P);
     if constexpr (ES == 4) {
       return reinterpret_cast<const float*>(S.win)[i];
     } else if constexpr (std::is_same_v<TL, __nv_bfloat16>) {
@@ -264,10 +281,12 @@ struct Step {
   }
 
   __device__ __forceinline__ bool flagged(const RowCtx& c, int tl) const {
+    const Smem S = smem_view(P);
     return c.pen_active && ((S.bitmap[tl >> 5] >> (tl & 31)) & 1u);
   }
 
   __device__ __forceinline__ int table_find(int tl) const {
+    const Smem S = smem_view(P);
     const int n = static_cast<int>(S.v->ntab);
     for (int j = 0; j < n; ++j)
       if (S.tab_tok[j] == tl) return j;
@@ -276,6 +295,7 @@ struct Step {
 
   // Exact value in the log-prob domain for local column tl whose raw logit is x.
   __device__ __forceinline__ float exact_y(const RowCtx& c, float x, int tl) const {
+    const Smem S = smem_view(P);
     if (P.mode == kModeProcessed) {
       if (c.excl && flagged(c, tl)) {
         const int j = table_find(tl);
@@ -309,6 +329,7 @@ struct Step {
   template <int N>
   __device__ __forceinline__ void process(const RowCtx& c, const float* x, int tb, bool valid, float& m, float& s,
                                           float thr_y, uint64_t thr_key) const {
+    const Smem S = smem_view(P);
     float y[N];
 #pragma unroll
     for (int i = 0; i < N; ++i) y[i] = (P.mode == kModeProcessed) ? x[i] * c.rteff : x[i];
@@ -359,14 +380,19 @@ struct Step {
   // ---- selection helpers ------------------------------------------------------
   // Reduce the shared key list to its best k (k < cnt).  Returns the cut.
   __device__ Cut shrink_to(int k) {
+    const Smem S = smem_view(P);
+    GR_PROF_T(t0);
     const int n = min(static_cast<int>(S.v->cnt), kKeyCap);
     uint64_t* keys = S.keys;
     Cut cut = cta_radix_select([keys](int i) { return keys[i]; }, n, k, S.sel);
     cta_compact(S.keys, n, cut, &S.v->cnt);
+    GR_PROF_ADD(8, t0);
+    GR_PROF_CNT(9);
     return cut;
   }
 
   __device__ void raise_tau(int r, uint64_t floor_key) {
+    const Smem S = smem_view(P);
     if (threadIdx.x == 0) {
       atomicMax(P.tau + r, static_cast<unsigned long long>(floor_key));
       if (floor_key > S.v->thr_key) S.v->thr_key = floor_key;
@@ -375,6 +401,7 @@ struct Step {
   }
 
   __device__ uint64_t min_key_of_list() {
+    const Smem S = smem_view(P);
     const int n = min(static_cast<int>(S.v->cnt), kKeyCap);
     uint64_t mn = ~0ull;
     for (int i = threadIdx.x; i < n; i += kThreads) mn = (S.keys[i] < mn) ? S.keys[i] : mn;
@@ -393,49 +420,135 @@ struct Step {
   }
 
   // ---- row-end candidate formation -----------------------------------------
-  __device__ void constrained_candidates(const RowCtx& c, float lse) {
-    constexpr int kPer = kBatch / kThreads;
-    for (int base = c.c0; base < c.c1; base += kBatch) {
-      const int end = min(base + kBatch, c.c1);
-      const uint64_t thr = S.v->thr_key;
-      // issue every child-token load of the batch before using any of them
-      int toks[kPer];
+  // Load window entries [i, i+8) (i a multiple of 8) as floats.
+  __device__ __forceinline__ void win_load8(int i, float* x) const {
+    const Smem S = smem_view(P);
+    if constexpr (ES == 4) {
+      const uint4 a = reinterpret_cast<const uint4*>(S.win)[i >> 2];
+      const uint4 b = reinterpret_cast<const uint4*>(S.win)[(i >> 2) + 1];
+      x[0] = __uint_as_float(a.x); x[1] = __uint_as_float(a.y); x[2] = __uint_as_float(a.z); x[3] = __uint_as_float(a.w);
+      x[4] = __uint_as_float(b.x); x[5] = __uint_as_float(b.y); x[6] = __uint_as_float(b.z); x[7] = __uint_as_float(b.w);
+    } else {
+      Tr::unpack(reinterpret_cast<const uint4*>(S.win)[i >> 3], x);
+    }
+  }
+
+  // Score one child candidate; returns its key (0 if not a local column).
+  __device__ __forceinline__ uint64_t child_key(const RowCtx& c, int tok, float x, float lse, uint32_t fb) const {
+    const float y = exact_y(c, x, tok - P.voff);
+    float sc = __fadd_rn(c.cum, __fsub_rn(y, lse));
+    if (tok == P.eos) {
+      if (P.eos_score) P.eos_score[c.row] = sc;
+      sc = -kInf;
+    }
+    return make_key(sc, fb + static_cast<uint32_t>(tok));
+  }
+
+  __device__ void constrained_candidates(const RowCtx& cref, float lse) {
+    const Smem S = smem_view(P);
+    const RowCtx c = cref;
+    const int c0 = c.c0, c1 = c.c1, deg = c1 - c0;
+    const uint32_t fb = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V);
+    // Scores of all children are compared against the threshold in float
+    // first; only the (rare) passers build keys and take part in the append.
+    // An exact float test is enough: key >= thr implies score >= score(thr).
+    const bool processed_div = (P.mode == kModeProcessed) && (c.excl || c.teff != 1.0f);
+    const bool dense_window = c.dense && !processed_div && (c.lo_tok - P.voff) == c.wlo && deg <= (c.whi - c.wlo + 1) &&
+                              (c.wlo & 7) == 0;
+    static_assert(kBatch == kThreads * 8, "dense path: one 8-entry group per thread per batch");
+    if (dense_window) {
+      // children are window entries [0, deg): 8 per thread per 16-byte load
+      for (int base = 0; base < deg; base += kBatch) {
+        const uint64_t thr = S.v->thr_key;
+        const float thr_s = thr ? key_score(thr) : -kInf;
+        const int i0 = base + static_cast<int>(threadIdx.x) * 8;   // kBatch == kThreads * 8
+        float x[8];
+        bool p[8];
+        bool any = false;
+        if (i0 < deg) {
+          win_load8(i0, x);
 #pragma unroll
-      for (int i = 0; i < kPer; ++i) {
-        const int j = base + i * kThreads + static_cast<int>(threadIdx.x);
-        toks[i] = (j < end) ? __ldg(P.child_tok + j) : -1;
-      }
+          for (int i = 0; i < 8; ++i) {
+            const float sc = __fadd_rn(c.cum, __fsub_rn(x[i], lse));
+            p[i] = (i0 + i < deg) && (sc >= thr_s || c.lo_tok + i0 + i == P.eos);
+            any |= p[i];
+          }
+        } else {
 #pragma unroll
-      for (int i = 0; i < kPer; ++i) {
-        if (base + i * kThreads >= end) break;           // uniform across the CTA
-        const int j = base + i * kThreads + static_cast<int>(threadIdx.x);
-        bool pred = false;
-        uint64_t key = 0;
-        if (j < end) {
-          const int tok = toks[i];
-          if (tok < 0 || tok >= P.V) {
-            atomicOr(P.err, GR_DEVERR_BAD_CHILD);
-          } else {
-            const int tl = tok - P.voff;
-            if (tl >= 0 && tl < P.VL) {
-              const float x = (tl >= c.wlo && tl <= c.whi) ? win_load(tl - c.wlo) : load_logit(c, tl);
-              const float y = exact_y(c, x, tl);
-              float sc = __fadd_rn(c.cum, __fsub_rn(y, lse));
-              if (tok == P.eos) {
-                if (P.eos_score) P.eos_score[c.row] = sc;
-                sc = -kInf;
-              }
-              key = make_key(sc, static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V) + static_cast<uint32_t>(tok));
+          for (int i = 0; i < 8; ++i) p[i] = false;
+        }
+        if (__any_sync(0xFFFFFFFFu, any)) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            uint64_t key = 0;
+            bool pred = p[i];
+            if (pred) {
+              key = child_key(c, c.lo_tok + i0 + i, x[i], lse, fb);
               pred = key >= thr;
             }
+            warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
           }
         }
-        warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
+        csync();
+        if (base + kBatch < deg && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
+          const Cut cut = shrink_to(P.k2);
+          raise_tau(c.r, cut.floor_key());
+        }
       }
-      csync();
-      if (end < c.c1 && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
-        const Cut cut = shrink_to(P.k2);
-        raise_tau(c.r, cut.floor_key());
+    } else {
+      constexpr int kPer = kBatch / kThreads;
+      for (int base = c0; base < c1; base += kBatch) {
+        const int end = min(base + kBatch, c1);
+        const uint64_t thr = S.v->thr_key;
+        const float thr_s = thr ? key_score(thr) : -kInf;
+        // issue every child-token load of the batch before using any of them
+        int toks[kPer];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int j = base + i * kThreads + static_cast<int>(threadIdx.x);
+          toks[i] = (j >= end) ? -1 : (c.dense ? c.lo_tok + (j - c0) : __ldg(P.child_tok + j));
+        }
+        float xs[kPer];
+        bool p[kPer];
+        bool any = false;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int tok = toks[i];
+          p[i] = false;
+          xs[i] = 0.0f;
+          if (tok >= 0) {
+            if (tok >= P.V) {
+              atomicOr(P.err, GR_DEVERR_BAD_CHILD);
+            } else {
+              const int tl = tok - P.voff;
+              if (tl >= 0 && tl < P.VL) {
+                const float x = (tl >= c.wlo && tl <= c.whi) ? win_load(tl - c.wlo) : load_logit(c, tl);
+                xs[i] = x;
+                const float y = exact_y(c, x, tl);
+                const float sc = __fadd_rn(c.cum, __fsub_rn(y, lse));
+                p[i] = (sc >= thr_s) || tok == P.eos;
+              }
+            }
+          }
+          any |= p[i];
+        }
+        if (__any_sync(0xFFFFFFFFu, any)) {
+#pragma unroll
+          for (int i = 0; i < kPer; ++i) {
+            uint64_t key = 0;
+            bool pred = p[i];
+            if (pred) {
+              key = child_key(c, toks[i], xs[i], lse, fb);
+              pred = key >= thr;
+            }
+            warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
+          }
+        }
+        csync();
+        if (end < c1 && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
+          const Cut cut = shrink_to(P.k2);
+          raise_tau(c.r, cut.floor_key());
+        }
       }
     }
     if (static_cast<int>(S.v->cnt) > P.k2) {
@@ -447,6 +560,7 @@ struct Step {
   // Streamed rows: convert the kept value-keys (ord(y) | ~flat) into score keys.
   // Returns false if the streamed boundary could hide a candidate.
   __device__ void unconstrained_candidates(const RowCtx& c, float lse) {
+    const Smem S = smem_view(P);
     // the kept set holds the row's best kk value-keys (all of them if nothing was discarded)
     if (static_cast<int>(S.v->cnt) > P.kk) {
       shrink_to(P.kk);
@@ -483,6 +597,7 @@ struct Step {
   // Reference-literal rows: the beam's own top-K by log-prob (vLLM topk),
   // de-duplicated against the greedy token, then masked to the catalog.
   __device__ void literal_candidates(const RowCtx& c, float lse) {
+    const Smem S = smem_view(P);
     if (static_cast<int>(S.v->cnt) > P.kk) {
       shrink_to(P.kk);
       if (threadIdx.x == 0) S.v->discard = 1;
@@ -580,8 +695,10 @@ struct Step {
     if (n > P.k2) shrink_to(P.k2);
   }
 
-  // Append the row's keys that beat the request threshold; returns nothing.
+  // Write the row's keys that beat the request threshold into the row's own
+  // slot of the candidate buffer (no atomics; the merge kernel gathers them).
   __device__ void emit(const RowCtx& c) {
+    const Smem S = smem_view(P);
     if (threadIdx.x == 0) {
       const uint64_t t = S.v->tau_pref;       // read at row start; a stale bound is still valid
       if (t > S.v->thr_key) S.v->thr_key = t;
@@ -590,97 +707,13 @@ struct Step {
     const uint64_t thr = S.v->thr_key;
     int n = min(static_cast<int>(S.v->cnt), kKeyCap);
     if (thr > 0 && n > 0) n = static_cast<int>(cta_compact(S.keys, n, Cut{thr, 0}, &S.v->cnt));
-    if (threadIdx.x == 0) S.v->base = n > 0 ? atomicAdd(P.cnt + c.r, static_cast<unsigned>(n)) : 0u;
-    csync();
-    const long long base = S.v->base;
-    if (threadIdx.x == 0 && base + n > P.cap) atomicOr(P.err, GR_DEVERR_OVERFLOW);
-    unsigned long long* dst = P.buf + static_cast<size_t>(c.r) * static_cast<size_t>(P.cap);
-    for (int i = threadIdx.x; i < n; i += kThreads)
-      if (base + i < P.cap) dst[base + i] = S.keys[i];
-  }
-
-  // The last CTA of request r: canonical top-2B, new beams and fork table.
-  __device__ void merge_request(int r) {
-    const unsigned long long* src = P.buf + static_cast<size_t>(r) * static_cast<size_t>(P.cap);
-    int n = static_cast<int>(*reinterpret_cast<volatile unsigned*>(P.cnt + r));
-    if (n > P.cap) n = static_cast<int>(P.cap);
-    const int k = min(P.k2, n);
-    if (threadIdx.x == 0) S.v->cnt = 0;
-    csync();
-    if (n > k) {
-      const Cut cut = cta_radix_select([src](int i) { return __ldcg(src + i); }, n, k, S.sel);
-      int dummy = 0;
-      for (int ib = warp_id() * 32; ib < n; ib += kThreads) {
-        const int i = ib + lane_id();
-        uint64_t key = 0;
-        bool pred = false;
-        if (i < n) {
-          key = __ldcg(src + i);
-          pred = cut.keep(key);
-        }
-        warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &dummy);
-      }
-    } else {
-      for (int i = threadIdx.x; i < n; i += kThreads) S.keys[i] = __ldcg(src + i);
+    if (n > P.k2) {                     // cannot happen: every path selects at most 2B
+      if (threadIdx.x == 0) atomicOr(P.err, GR_DEVERR_OVERFLOW);
+      n = P.k2;
     }
-    csync();
-    int P2 = 1;
-    while (P2 < k) P2 <<= 1;
-    for (int i = k + threadIdx.x; i < P2; i += kThreads) S.keys[i] = 0ull;
-    csync();
-    cta_bitonic_sort_desc(S.keys, P2);
-    const int B = P.B, k2 = P.k2, NB = P.NB, T = P.T;
-    for (int i = threadIdx.x; i < k2; i += kThreads) {
-      float sc = -kInf;
-      int tok = -1, par = -1;
-      if (i < k) {
-        const uint64_t key = S.keys[i];
-        const uint32_t flat = key_flat(key);
-        sc = key_score(key);
-        tok = static_cast<int>(flat % static_cast<uint32_t>(P.V));
-        par = static_cast<int>(flat / static_cast<uint32_t>(P.V));
-      }
-      P.cand_score[static_cast<size_t>(r) * k2 + i] = sc;
-      P.cand_token[static_cast<size_t>(r) * k2 + i] = tok;
-      P.cand_parent[static_cast<size_t>(r) * k2 + i] = par;
-      if (i < B) {
-        P.sel_score[static_cast<size_t>(r) * B + i] = sc;
-        P.sel_token[static_cast<size_t>(r) * B + i] = tok;
-        P.sel_parent[static_cast<size_t>(r) * B + i] = par;
-        int child = GR_NODE_DEAD;
-        if (par >= 0) {
-          const int pn = P.node[r * NB + par];
-          if (pn == GR_NODE_UNCONSTRAINED) {
-            child = GR_NODE_UNCONSTRAINED;
-          } else if (pn >= 0 && pn < P.N) {
-            int lo = static_cast<int>(P.row_ptr[pn]);
-            const int hi0 = static_cast<int>(P.row_ptr[pn + 1]);
-            int hi = hi0;
-            while (lo < hi) {
-              const int mid = (lo + hi) >> 1;
-              if (P.child_tok[mid] < tok) lo = mid + 1; else hi = mid;
-            }
-            if (lo < hi0 && P.child_tok[lo] == tok) child = P.child_node[lo];
-          }
-        }
-        P.sel_node[static_cast<size_t>(r) * B + i] = child;
-      }
-    }
-    if (P.hist_out) {
-      const int W = T + 1;
-      for (int idx = threadIdx.x; idx < B * W; idx += kThreads) {
-        const int i = idx / W, t = idx - i * W;
-        int v = -1;
-        if (i < k) {
-          const uint32_t flat = key_flat(S.keys[i]);
-          const int par = static_cast<int>(flat / static_cast<uint32_t>(P.V));
-          v = (t < T) ? P.hist[(static_cast<size_t>(r) * NB + par) * T + t]
-                      : static_cast<int>(flat % static_cast<uint32_t>(P.V));
-        }
-        P.hist_out[static_cast<size_t>(r) * B * W + idx] = v;
-      }
-    }
-    csync();
+    unsigned long long* dst = P.buf + static_cast<size_t>(c.row) * static_cast<size_t>(P.k2);
+    for (int i = threadIdx.x; i < n; i += kThreads) dst[i] = S.keys[i];
+    if (threadIdx.x == 0) P.rowcnt[c.row] = static_cast<unsigned>(n);
   }
 };
 
@@ -744,7 +777,8 @@ struct FastSum<float> {
 
 // Producer warp, lane 0: fill the ring with the CTA's (row, chunk) sequence.
 template <int ES>
-__device__ void produce(const Params& P, Smem& S, int my_n) {
+__device__ __forceinline__ void produce(const Params& P, int my_n) {
+  const Smem S = smem_view(P);
   const uint64_t pol = l2_policy_evict_first();
   int stage = 0;
   uint32_t round = 0;
@@ -781,9 +815,8 @@ done:
 
 template <typename TL>
 __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_constant__ Params P) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  Smem S = carve(smem_raw, P);
-  Step<TL> st(P, S);
+  const Smem S = smem_view(P);
+  Step<TL> st(P);
   using Tr = LogitTraits<TL>;
   constexpr int ES = sizeof(TL);
   constexpr int EPV = Tr::kPerVec;
@@ -810,15 +843,17 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
   __syncthreads();   // the only CTA-wide barrier: consumers use csync() from here on
 
   if (warp == kWarps) {
-    if (lane == 0) produce<ES>(P, S, my_n);
+    if (lane == 0) produce<ES>(P, my_n);
     return;
   }
 
   int cstage = 0;
   uint32_t cphase = 0;
   long long consumed = 0;
+  GR_PROF_T(t_kernel);
   for (int it = 0; it < my_n; ++it) {
     // ------------------------------------------------------------ row setup
+    GR_PROF_CNT(10);
     RowCtx c;
     c.row = row_of_iter(P, it);
     c.r = c.row / P.NB;
@@ -837,9 +872,14 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
     }
     c.wlo = 1;
     c.whi = 0;
+    c.lo_tok = 0;
+    c.dense = false;
     if (c.constrained && c.c1 > c.c0) {
-      const int lo = max(P.child_tok[c.c0] - P.voff, 0);
-      const int hi = min(P.child_tok[c.c1 - 1] - P.voff, P.VL - 1);
+      const int lt = P.child_tok[c.c0], ht = P.child_tok[c.c1 - 1];
+      c.lo_tok = lt;
+      c.dense = (ht - lt + 1) == (c.c1 - c.c0);
+      const int lo = max(lt - P.voff, 0);
+      const int hi = min(ht - P.voff, P.VL - 1);
       if (lo <= hi) {
         c.wlo = lo;
         c.whi = min(hi, lo + Step<TL>::kWinTok - 1);
@@ -922,11 +962,14 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
     }
 
     // ------------------------------------------------------------ body chunks
+    GR_PROF_T(t_stream);
     for (int ch = 0; ch < g.nchunks; ++ch) {
+      GR_PROF_T(t_wait);
       if (!mbar_wait_bounded(&S.full[cstage], cphase, &S.v->abort)) {
         if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
         S.v->abort = 1;
       }
+      GR_PROF_ADD(1, t_wait);
       const long long off = static_cast<long long>(ch) * kStageBytes;
       const int bytes = static_cast<int>(min(static_cast<long long>(kStageBytes), g.body_bytes - off));
       const int nvec = bytes >> 4;
@@ -1025,6 +1068,8 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
     }
 
     fold(sacc0, sacc1, s);
+    GR_PROF_ADD(0, t_stream);
+    GR_PROF_T(t_red);
 
     // ------------------------------------------------------------ row end
     if (c.excl) {
@@ -1079,8 +1124,10 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
       if (P.partial_only) P.partials[c.row] = make_float2(M, tot);
     }
     csync();
+    GR_PROF_ADD(2, t_red);
     if (S.v->abort) goto drain;
     const float lse = S.v->lse;
+    GR_PROF_T(t_cand);
 
     if (!P.partial_only) {
       if (tid == 0) S.v->tau_pref = tau_pref;
@@ -1093,6 +1140,8 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
       } else if (c.stream) {
         st.literal_candidates(c, lse);
       }
+      GR_PROF_ADD(3, t_cand);
+      GR_PROF_T(t_emit);
       if (tid == 0 && S.v->overflow) atomicOr(P.err, GR_DEVERR_OVERFLOW);
       if (c.stream) {
         // the row-local threshold was over value keys; only the request bound applies now
@@ -1100,17 +1149,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
         csync();
       }
       st.emit(c);
-      __threadfence();
-      csync();
-      if (tid == 0) {
-        const unsigned prev = atomicAdd(P.done + c.r, 1u);
-        S.v->last = (prev == static_cast<unsigned>(P.NB - 1)) ? 1 : 0;
-      }
-      csync();
-      if (S.v->last) {
-        __threadfence();
-        st.merge_request(c.r);
-      }
+      GR_PROF_ADD(4, t_emit);
     }
     if (c.pen_active) {
       const int nt = static_cast<int>(S.v->ntab);
@@ -1118,6 +1157,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
     }
     csync();
   }
+  GR_PROF_ADD(11, t_kernel);
   return;
 
 drain:
@@ -1140,6 +1180,161 @@ drain:
   csync();
 }
 
+// ---------------------------------------------------------------- merge kernel
+// One CTA of kThreads threads per request: gathers the request's per-row
+// candidate slots, keeps the canonical top-2B (radix select over the keys),
+// sorts them and writes candidates, new beams with their child trie nodes and
+// the forked token table (serving_engine.py:566-590, llm.py:256-276).
+constexpr int kMergeMaxBeams = 4096;
+
+struct MergeSmem {
+  uint64_t* keys;      // [kKeyCap]
+  uint32_t* prefix;    // [NB + 1] exclusive prefix of the row counts
+  SelectScratch* sel;
+  uint32_t* wsum;      // [kWarps]
+  uint32_t* cnt;
+};
+
+__host__ __device__ inline size_t merge_smem_bytes(int NB) {
+  return align128(size_t(kKeyCap) * 8) + align128(size_t(NB + 1) * 4) + align128(sizeof(SelectScratch)) +
+         align128(kWarps * 4) + 128;
+}
+
+__device__ __forceinline__ int row_of_index(const uint32_t* prefix, int NB, uint32_t i) {
+  int lo = 0, hi = NB;                 // prefix[lo] <= i < prefix[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (prefix[mid] <= i) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__ Params P) {
+  unsigned char* smem_raw = g_smem;
+  MergeSmem M;
+  {
+    size_t o = 0;
+    M.keys = reinterpret_cast<uint64_t*>(smem_raw + o); o += align128(size_t(kKeyCap) * 8);
+    M.prefix = reinterpret_cast<uint32_t*>(smem_raw + o); o += align128(size_t(P.NB + 1) * 4);
+    M.sel = reinterpret_cast<SelectScratch*>(smem_raw + o); o += align128(sizeof(SelectScratch));
+    M.wsum = reinterpret_cast<uint32_t*>(smem_raw + o); o += align128(kWarps * 4);
+    M.cnt = reinterpret_cast<uint32_t*>(smem_raw + o);
+  }
+  const int r = blockIdx.x, tid = threadIdx.x, lane = lane_id(), warp = warp_id();
+  const int NB = P.NB, k2 = P.k2;
+  // ---- exclusive prefix of the per-row counts
+  const unsigned* cnt = P.rowcnt + static_cast<size_t>(r) * NB;
+  const int per = (NB + kThreads - 1) / kThreads;
+  const int b0 = min(tid * per, NB), b1 = min(b0 + per, NB);
+  uint32_t local = 0;
+  for (int b = b0; b < b1; ++b) local += min(__ldcg(cnt + b), static_cast<unsigned>(k2));
+  uint32_t inc = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += v;
+  }
+  if (lane == 31) M.wsum[warp] = inc;
+  csync();
+  if (tid == 0) {
+    uint32_t acc = 0;
+    for (int w = 0; w < kWarps; ++w) {
+      const uint32_t t = M.wsum[w];
+      M.wsum[w] = acc;
+      acc += t;
+    }
+    M.prefix[NB] = acc;
+    *M.cnt = 0;
+  }
+  csync();
+  uint32_t base = M.wsum[warp] + inc - local;
+  for (int b = b0; b < b1; ++b) {
+    M.prefix[b] = base;
+    base += min(__ldcg(cnt + b), static_cast<unsigned>(k2));
+  }
+  csync();
+  const int n = static_cast<int>(M.prefix[NB]);
+  const int k = min(k2, n);
+  const unsigned long long* slots = P.buf + static_cast<size_t>(r) * NB * static_cast<size_t>(k2);
+  const uint32_t* prefix = M.prefix;
+  auto keyf = [slots, prefix, NB, k2](int i) -> uint64_t {
+    const int b = row_of_index(prefix, NB, static_cast<uint32_t>(i));
+    return __ldcg(slots + static_cast<size_t>(b) * k2 + (static_cast<uint32_t>(i) - prefix[b]));
+  };
+  // ---- canonical top-2B
+  Cut cut{0ull, 0};
+  if (n > k) cut = cta_radix_select(keyf, n, k, M.sel);
+  int dummy = 0;
+  for (int ib = warp * 32; ib < n; ib += kThreads) {
+    const int i = ib + lane;
+    uint64_t key = 0;
+    bool pred = false;
+    if (i < n) {
+      key = keyf(i);
+      pred = (n <= k) || cut.keep(key);
+    }
+    warp_append(pred, key, M.keys, M.cnt, kKeyCap, &dummy);
+  }
+  csync();
+  int P2 = 1;
+  while (P2 < k) P2 <<= 1;
+  for (int i = k + tid; i < P2; i += kThreads) M.keys[i] = 0ull;
+  csync();
+  cta_bitonic_sort_desc(M.keys, P2);
+  // ---- outputs
+  const int B = P.B, T = P.T;
+  for (int i = tid; i < k2; i += kThreads) {
+    float sc = -kInf;
+    int tok = -1, par = -1;
+    if (i < k) {
+      const uint64_t key = M.keys[i];
+      const uint32_t flat = key_flat(key);
+      sc = key_score(key);
+      tok = static_cast<int>(flat % static_cast<uint32_t>(P.V));
+      par = static_cast<int>(flat / static_cast<uint32_t>(P.V));
+    }
+    P.cand_score[static_cast<size_t>(r) * k2 + i] = sc;
+    P.cand_token[static_cast<size_t>(r) * k2 + i] = tok;
+    P.cand_parent[static_cast<size_t>(r) * k2 + i] = par;
+    if (i < B) {
+      P.sel_score[static_cast<size_t>(r) * B + i] = sc;
+      P.sel_token[static_cast<size_t>(r) * B + i] = tok;
+      P.sel_parent[static_cast<size_t>(r) * B + i] = par;
+      int child = GR_NODE_DEAD;
+      if (par >= 0) {
+        const int pn = P.node[r * NB + par];
+        if (pn == GR_NODE_UNCONSTRAINED) {
+          child = GR_NODE_UNCONSTRAINED;
+        } else if (pn >= 0 && pn < P.N) {
+          int lo = static_cast<int>(P.row_ptr[pn]);
+          const int hi0 = static_cast<int>(P.row_ptr[pn + 1]);
+          int hi = hi0;
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (P.child_tok[mid] < tok) lo = mid + 1; else hi = mid;
+          }
+          if (lo < hi0 && P.child_tok[lo] == tok) child = P.child_node[lo];
+        }
+      }
+      P.sel_node[static_cast<size_t>(r) * B + i] = child;
+    }
+  }
+  if (P.hist_out) {
+    const int W = T + 1;
+    for (int idx = tid; idx < B * W; idx += kThreads) {
+      const int i = idx / W, t = idx - i * W;
+      int v = -1;
+      if (i < k) {
+        const uint32_t flat = key_flat(M.keys[i]);
+        const int par = static_cast<int>(flat / static_cast<uint32_t>(P.V));
+        v = (t < T) ? P.hist[(static_cast<size_t>(r) * NB + par) * T + t]
+                    : static_cast<int>(flat % static_cast<uint32_t>(P.V));
+      }
+      P.hist_out[static_cast<size_t>(r) * B * W + idx] = v;
+    }
+  }
+}
+
 // ============================================================== host side
 struct DeviceInfo {
   int sms = 0;
@@ -1148,6 +1343,7 @@ struct DeviceInfo {
   int smem_reserved = 0;
   int major = 0;
   bool attr_set[3] = {false, false, false};
+  bool merge_attr_set = false;
 };
 
 static DeviceInfo g_dev[64];
@@ -1178,7 +1374,9 @@ static int device_info(DeviceInfo** out) {
   return GR_OK;
 }
 
-static size_t ws_header_bytes(int R) { return align128(size_t(R) * 16); }
+// Workspace: tau [R] u64 | row counts [R*NB] u32 | row slots [R*NB][2B] u64.
+static size_t ws_tau_bytes(int R) { return align128(size_t(R) * 8); }
+static size_t ws_cnt_bytes(int R, int NB) { return align128(size_t(R) * NB * 4); }
 
 static int validate(const gr_step_desc* d) {
   if (!d) return GR_ERR_NULL;
@@ -1201,6 +1399,7 @@ static int validate(const gr_step_desc* d) {
   const int kk = (k2 > d->per_beam_k ? k2 : d->per_beam_k) + kSlack;
   if (kk > kKeyCap - kBatch) return GR_ERR_UNSUPPORTED;
   if (d->num_edges > 0x7FFFFFFFll) return GR_ERR_UNSUPPORTED;
+  if (d->num_beams > kMergeMaxBeams) return GR_ERR_UNSUPPORTED;
   return GR_OK;
 }
 
@@ -1296,6 +1495,20 @@ static int launch_fused(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream_t 
   return GR_OK;
 }
 
+static int launch_merge(const Params& P, DeviceInfo* dev, cudaStream_t stream) {
+  const size_t smem = merge_smem_bytes(P.NB);
+  if (smem > static_cast<size_t>(dev->smem_optin)) return GR_ERR_UNSUPPORTED;
+  if (!dev->merge_attr_set) {
+    if (cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dev->smem_optin) !=
+        cudaSuccess)
+      return GR_ERR_CUDA;
+    dev->merge_attr_set = true;
+  }
+  merge_kernel<<<P.R, kThreads, smem, stream>>>(P);
+  if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
+  return GR_OK;
+}
+
 static int launch_by_dtype(Params& P, int dtype, DeviceInfo* dev, cudaStream_t stream) {
   switch (dtype) {
     case GR_DTYPE_F32: return launch_fused<float>(P, dev, 0, stream);
@@ -1332,8 +1545,8 @@ int32_t gr_beam_step_workspace_size(const gr_step_desc* d, size_t* bytes) {
   if (!d || !bytes) return GR_ERR_NULL;
   const int v = validate(d);
   if (v != GR_OK) return v;
-  const size_t cap = size_t(d->num_beams) * size_t(2 * d->beam_width);
-  *bytes = ws_header_bytes(d->num_requests) + align128(size_t(d->num_requests) * cap * 8);
+  const size_t slots = size_t(d->num_requests) * d->num_beams * size_t(2 * d->beam_width);
+  *bytes = ws_tau_bytes(d->num_requests) + ws_cnt_bytes(d->num_requests, d->num_beams) + align128(slots * 8);
   return GR_OK;
 }
 
@@ -1364,14 +1577,25 @@ int32_t gr_beam_step(const gr_step_desc* d, const gr_step_io* io, void* workspac
   const int R = d->num_requests;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   P.tau = reinterpret_cast<unsigned long long*>(ws);
-  P.cnt = reinterpret_cast<unsigned int*>(ws + size_t(R) * 8);
-  P.done = reinterpret_cast<unsigned int*>(ws + size_t(R) * 12);
-  P.buf = reinterpret_cast<unsigned long long*>(ws + ws_header_bytes(R));
-  P.cap = static_cast<long long>(d->num_beams) * (2 * d->beam_width);
+  P.rowcnt = reinterpret_cast<unsigned int*>(ws + ws_tau_bytes(R));
+  P.buf = reinterpret_cast<unsigned long long*>(ws + ws_tau_bytes(R) + ws_cnt_bytes(R, d->num_beams));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(ws, 0, size_t(R) * 16, s) != cudaSuccess) return GR_ERR_CUDA;
-  return launch_by_dtype(P, d->logit_dtype, dev, s);
+  if (cudaMemsetAsync(ws, 0, size_t(R) * 8, s) != cudaSuccess) return GR_ERR_CUDA;
+  v = launch_by_dtype(P, d->logit_dtype, dev, s);
+  if (v != GR_OK) return v;
+  return launch_merge(P, dev, s);
 }
+
+#ifdef GR_PHASE_PROFILE
+// Debug builds only: copy and clear the per-CTA phase counters.
+int32_t gr_debug_phase_counters(void* host, size_t bytes) {
+  if (bytes < sizeof(g_phase)) return GR_ERR_WORKSPACE;
+  if (cudaMemcpyFromSymbol(host, g_phase, sizeof(g_phase)) != cudaSuccess) return GR_ERR_CUDA;
+  static unsigned long long zeros[1024][kProfSlots];
+  if (cudaMemcpyToSymbol(g_phase, zeros, sizeof(g_phase)) != cudaSuccess) return GR_ERR_CUDA;
+  return GR_OK;
+}
+#endif
 
 int32_t gr_lse_partials(const gr_step_desc* d, const void* logits, const float* temperature,
                         const float* rep_penalty, const float* pres_penalty, const float* freq_penalty,
