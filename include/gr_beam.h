@@ -157,6 +157,26 @@ int32_t gr_beam_step_workspace_size(const gr_step_desc* desc, size_t* bytes);
 int32_t gr_beam_step(const gr_step_desc* desc, const gr_step_io* io,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the device scratch built into the library for gr_beam_step_noalloc. */
+#define GR_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* The same step as gr_beam_step, for callers that cannot allocate device
+ * memory (for example code running where a cudaMalloc would synchronise the
+ * device or break a memory pool's accounting, or hosts with no allocator of
+ * their own): it takes no workspace and allocates nothing.  It uses a fixed
+ * GR_NOALLOC_SCRATCH_BYTES array of device memory that the library holds on
+ * every GPU it is loaded on, until the process exits.
+ *   - Requests whose gr_beam_step_workspace_size exceeds that size are
+ *     rejected with GR_ERR_WORKSPACE (use gr_beam_step with your own
+ *     workspace for them).
+ *   - The first call on a device looks up the array's device address (with
+ *     that device current); make that first call before any stream capture.
+ *   - All calls share the one array: calls that may run at the same time on
+ *     the GPU (different streams, different host threads) race on it and must
+ *     be serialised by the caller.
+ * No counterpart in the reference (an addition of this library). */
+int32_t gr_beam_step_noalloc(const gr_step_desc* desc, const gr_step_io* io, void* stream);
+
 /* ---- vocab-sharded lm_head (logit columns split over ranks) --------------
  *
  * Phase 1 (every shard): per-row partial (max, sum exp(x - max)) over the

@@ -26,8 +26,9 @@ NODE_UNCONSTRAINED, NODE_DEAD = -1, -2
 
 EXPORTED_SYMBOLS = (
     "gr_abi_version", "gr_status_string", "gr_beam_step_workspace_size", "gr_beam_step",
-    "gr_lse_partials", "gr_shard_candidates", "gr_merge_candidates",
+    "gr_lse_partials", "gr_shard_candidates", "gr_merge_candidates", "gr_beam_step_noalloc",
 )
+NOALLOC_SCRATCH_BYTES = 16 << 20
 
 
 class StepDesc(ctypes.Structure):
@@ -86,6 +87,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
     lib.gr_beam_step_workspace_size.argtypes = [P(StepDesc), P(ctypes.c_size_t)]
     lib.gr_beam_step.restype = ctypes.c_int32
     lib.gr_beam_step.argtypes = [P(StepDesc), P(StepIO), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.gr_beam_step_noalloc.restype = ctypes.c_int32
+    lib.gr_beam_step_noalloc.argtypes = [P(StepDesc), P(StepIO), ctypes.c_void_p]
     lib.gr_lse_partials.restype = ctypes.c_int32
     lib.gr_lse_partials.argtypes = [P(StepDesc), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,

@@ -21,6 +21,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cuda_runtime.h>
+#include <mutex>
 #include <type_traits>
 
 #include "../../include/gr_beam.h"
@@ -1596,6 +1597,46 @@ int32_t gr_debug_phase_counters(void* host, size_t bytes) {
   return GR_OK;
 }
 #endif
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ no-alloc
+// Scratch for gr_beam_step_noalloc: a fixed array in device memory that every
+// GPU loading this library holds until the process exits.  Host code must not
+// pass `g_noalloc_scratch` itself to a kernel (on the host it only names the
+// symbol); the device address comes from cudaGetSymbolAddress, once per device.
+namespace gr {
+constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(GR_NOALLOC_SCRATCH_BYTES);
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static void* g_noalloc_ptr[64];
+static std::mutex g_noalloc_mu;
+}  // namespace gr
+
+extern "C" {
+
+int32_t gr_beam_step_noalloc(const gr_step_desc* d, const gr_step_io* io, void* stream) {
+  if (!d || !io) return GR_ERR_NULL;
+  size_t need = 0;
+  const int v = gr_beam_step_workspace_size(d, &need);
+  if (v != GR_OK) return v;
+  if (need > kNoAllocScratchBytes) return GR_ERR_WORKSPACE;    // beyond the built-in scratch
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GR_ERR_NO_DEVICE;
+  void* ptr = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    ptr = g_noalloc_ptr[dev];
+    if (ptr == nullptr) {
+      // first call on this device (current device = dev): resolve the array's device address
+      if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return GR_ERR_CUDA;
+      g_noalloc_ptr[dev] = ptr;
+    }
+  }
+  // gr_beam_step clears the part of the scratch that must start at zero (the
+  // per-request thresholds); every other byte it reads is written earlier in
+  // the same call.
+  return gr_beam_step(d, io, ptr, kNoAllocScratchBytes, stream);
+}
 
 int32_t gr_lse_partials(const gr_step_desc* d, const void* logits, const float* temperature,
                         const float* rep_penalty, const float* pres_penalty, const float* freq_penalty,
