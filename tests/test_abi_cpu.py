@@ -1,0 +1,94 @@
+"""C ABI on the CPU: the library loads without a GPU, exports every function
+the header declares, its structs have the header's layout, and descriptor
+validation answers without touching a device."""
+import ctypes
+import os
+import re
+import subprocess
+import tempfile
+
+import pytest
+
+from vllm_gr_ehaleva_b200 import _lib
+from vllm_gr_ehaleva_b200.sample.beam_search_sampler import make_desc
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gr_beam.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int32_t|const char\*)\s+(gr_\w+)\s*\(", text, re.M)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 8
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in gr_beam.h but not exported"
+    assert set(_lib.EXPORTED_SYMBOLS) == set(names)
+    assert lib.gr_abi_version() == 1
+    assert lib.gr_status_string(-6) == b"GR_ERR_UNSUPPORTED"
+
+
+def test_struct_layout_matches_header():
+    src = r'''
+#include <stdio.h>
+#include <stddef.h>
+#include "gr_beam.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu %zu\n", sizeof(gr_step_desc), sizeof(gr_step_io),
+         offsetof(gr_step_desc, row_stride), offsetof(gr_step_desc, num_edges),
+         offsetof(gr_step_io, cand_score), offsetof(gr_step_io, err));
+  return 0;
+}
+'''
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "probe.c")
+        exe = os.path.join(d, "probe")
+        open(c, "w").write(src)
+        subprocess.run(["gcc", "-I", os.path.dirname(HEADER), c, "-o", exe], check=True)
+        got = list(map(int, subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()))
+    want = [ctypes.sizeof(_lib.StepDesc), ctypes.sizeof(_lib.StepIO), _lib.StepDesc.row_stride.offset,
+            _lib.StepDesc.num_edges.offset, _lib.StepIO.cand_score.offset, _lib.StepIO.err.offset]
+    assert got == want
+
+
+def _desc(**kw):
+    base = dict(R=2, NB=4, B=4, V=1000, VL=1000, voff=0, row_stride=1000, dtype=1, mode=0, K=0, eos=-1, T=0, N=0, E=0)
+    base.update(kw)
+    return make_desc(**base)
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(), 0),
+    (dict(R=0), -2), (dict(NB=0), -2), (dict(B=0), -2),
+    (dict(VL=1001), -2), (dict(voff=10), -2), (dict(row_stride=999), -2),
+    (dict(dtype=7), -3), (dict(mode=3), -3),
+    (dict(K=2000), -2), (dict(eos=1000), -2),
+    (dict(B=3000), -6),                           # 2B beyond the shared-memory key list
+    (dict(NB=100000, V=100000, VL=100000, row_stride=100000), -6),   # flat index beyond 32 bits
+])
+def test_workspace_size_validation(kw, status):
+    lib = _lib.load()
+    n = ctypes.c_size_t(0)
+    assert lib.gr_beam_step_workspace_size(ctypes.byref(_desc(**kw)), ctypes.byref(n)) == status
+    if status == 0:
+        # tau [R] + row counts [R*NB] + row slots [R*NB][2B] (128-byte aligned pieces)
+        assert n.value >= 2 * 8 + 2 * 4 * 4 + 2 * 4 * 8 * 8
+
+
+def test_null_arguments_rejected_before_any_device_work():
+    lib = _lib.load()
+    d = _desc()
+    io = _lib.StepIO()
+    assert lib.gr_beam_step(None, ctypes.byref(io), None, 0, None) == -1
+    assert lib.gr_beam_step(ctypes.byref(d), ctypes.byref(io), None, 0, None) == -1   # logits missing
+    assert lib.gr_beam_step_noalloc(None, None, None) == -1
+
+
+def test_sampler_refuses_to_run_without_the_library(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "_lib", None)
+    with pytest.raises(ImportError):
+        _lib.load(str(tmp_path / "missing.so"))
