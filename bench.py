@@ -293,7 +293,7 @@ def run_ours(args):
                      "algorithmic_bytes_per_launch": int(np.mean(steps_bytes)),
                      "avg_launch_ms": round(avg_launch_ms, 5), "per_level_ms": per_level_ms,
                      "per_level_bytes": [int(b) for b in bytes_cycle]},
-        "gpu_launches": args.steps,
+        "gpu_launches": 2 * args.steps,          # fused_step_kernel + merge_kernel per step
         "clocks": clk,
         "device_errors": err,
     }
@@ -301,15 +301,13 @@ def run_ours(args):
         res["e2e"] = e2e
     if cpu is not None:
         res["cpu_baseline"] = cpu
-    prof = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(prof):
-        try:
-            with open(prof) as f:
-                tr = json.load(f).get(args.config)
-            if tr:
-                res["roofline"]["traffic"] = tr
-        except Exception:
-            pass
+    # DRAM traffic per launch from the committed ncu summary (same kernel, same workload)
+    prof = os.path.join(ROOT, "profiles", f"fused_step_{args.config}.md")
+    if os.path.exists(prof) and R == CONFIGS[args.config]["requests"]:
+        with open(prof) as f:
+            for line in f:
+                if line.startswith(f"traffic_bytes_per_launch_{args.config}:"):
+                    res["roofline"]["traffic"] = int(line.split(":")[1])
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

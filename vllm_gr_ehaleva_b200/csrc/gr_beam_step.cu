@@ -1187,9 +1187,10 @@ drain:
 // sorts them and writes candidates, new beams with their child trie nodes and
 // the forked token table (serving_engine.py:566-590, llm.py:256-276).
 constexpr int kMergeMaxBeams = 4096;
+constexpr int kMergeCap = 16384;     // request candidates gathered into shared memory at once
 
 struct MergeSmem {
-  uint64_t* keys;      // [kKeyCap]
+  uint64_t* keys;      // [kMergeCap]
   uint32_t* prefix;    // [NB + 1] exclusive prefix of the row counts
   SelectScratch* sel;
   uint32_t* wsum;      // [kWarps]
@@ -1197,7 +1198,7 @@ struct MergeSmem {
 };
 
 __host__ __device__ inline size_t merge_smem_bytes(int NB) {
-  return align128(size_t(kKeyCap) * 8) + align128(size_t(NB + 1) * 4) + align128(sizeof(SelectScratch)) +
+  return align128(size_t(kMergeCap) * 8) + align128(size_t(NB + 1) * 4) + align128(sizeof(SelectScratch)) +
          align128(kWarps * 4) + 128;
 }
 
@@ -1215,7 +1216,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
   MergeSmem M;
   {
     size_t o = 0;
-    M.keys = reinterpret_cast<uint64_t*>(smem_raw + o); o += align128(size_t(kKeyCap) * 8);
+    M.keys = reinterpret_cast<uint64_t*>(smem_raw + o); o += align128(size_t(kMergeCap) * 8);
     M.prefix = reinterpret_cast<uint32_t*>(smem_raw + o); o += align128(size_t(P.NB + 1) * 4);
     M.sel = reinterpret_cast<SelectScratch*>(smem_raw + o); o += align128(sizeof(SelectScratch));
     M.wsum = reinterpret_cast<uint32_t*>(smem_raw + o); o += align128(kWarps * 4);
@@ -1263,20 +1264,44 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     return __ldcg(slots + static_cast<size_t>(b) * k2 + (static_cast<uint32_t>(i) - prefix[b]));
   };
   // ---- canonical top-2B
-  Cut cut{0ull, 0};
-  if (n > k) cut = cta_radix_select(keyf, n, k, M.sel);
   int dummy = 0;
-  for (int ib = warp * 32; ib < n; ib += kThreads) {
-    const int i = ib + lane;
-    uint64_t key = 0;
-    bool pred = false;
-    if (i < n) {
-      key = keyf(i);
-      pred = (n <= k) || cut.keep(key);
+  if (n <= kMergeCap) {
+    // gather every row slot into shared memory (one warp per row, coalesced)
+    for (int b = warp; b < NB; b += kWarps) {
+      const int c = static_cast<int>(M.prefix[b + 1] - M.prefix[b]);
+      const unsigned long long* src = slots + static_cast<size_t>(b) * k2;
+      uint64_t* dst = M.keys + M.prefix[b];
+      for (int j = lane; j < c; j += 32) dst[j] = __ldcg(src + j);
     }
-    warp_append(pred, key, M.keys, M.cnt, kKeyCap, &dummy);
+    csync();
+    if (n > k) {
+      uint64_t* keys = M.keys;
+      const Cut cut = cta_radix_select([keys](int i) { return keys[i]; }, n, k, M.sel);
+      // compact in rounds of one key per thread: writes never pass the keys read so far
+      for (int base = 0; base < n; base += kThreads) {
+        const int i = base + tid;
+        const uint64_t key = (i < n) ? keys[i] : 0ull;
+        const bool keep = (i < n) && cut.keep(key);
+        csync();
+        warp_append(keep, key, keys, M.cnt, kMergeCap, &dummy);
+      }
+      csync();
+    }
+  } else {
+    Cut cut{0ull, 0};
+    if (n > k) cut = cta_radix_select(keyf, n, k, M.sel);
+    for (int ib = warp * 32; ib < n; ib += kThreads) {
+      const int i = ib + lane;
+      uint64_t key = 0;
+      bool pred = false;
+      if (i < n) {
+        key = keyf(i);
+        pred = (n <= k) || cut.keep(key);
+      }
+      warp_append(pred, key, M.keys, M.cnt, kMergeCap, &dummy);
+    }
+    csync();
   }
-  csync();
   int P2 = 1;
   while (P2 < k) P2 <<= 1;
   for (int i = k + tid; i < P2; i += kThreads) M.keys[i] = 0ull;
