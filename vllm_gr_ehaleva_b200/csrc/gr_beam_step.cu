@@ -454,24 +454,26 @@ struct Step {
     // first; only the (rare) passers build keys and take part in the append.
     // An exact float test is enough: key >= thr implies score >= score(thr).
     const bool processed_div = (P.mode == kModeProcessed) && (c.excl || c.teff != 1.0f);
-    const bool dense_window = c.dense && !processed_div && (c.lo_tok - P.voff) == c.wlo && deg <= (c.whi - c.wlo + 1) &&
-                              (c.wlo & 7) == 0;
+    const int first = c.lo_tok - P.voff;
+    const bool dense_window = c.dense && !processed_div && first >= c.wlo && first + deg - 1 <= c.whi;
+    const int d0 = first - c.wlo;               // window index of the first child
     static_assert(kBatch == kThreads * 8, "dense path: one 8-entry group per thread per batch");
     if (dense_window) {
-      // children are window entries [0, deg): 8 per thread per 16-byte load
-      for (int base = 0; base < deg; base += kBatch) {
+      // child j sits at window index d0 + j: 8 window entries per thread per 16-byte load
+      for (int base = 0; base < d0 + deg; base += kBatch) {
         const uint64_t thr = S.v->thr_key;
         const float thr_s = thr ? key_score(thr) : -kInf;
-        const int i0 = base + static_cast<int>(threadIdx.x) * 8;   // kBatch == kThreads * 8
+        const int w0 = base + static_cast<int>(threadIdx.x) * 8;   // kBatch == kThreads * 8
+        const int i0 = w0 - d0;                                     // child index of entry w0
         float x[8];
         bool p[8];
         bool any = false;
-        if (i0 < deg) {
-          win_load8(i0, x);
+        if (w0 < d0 + deg) {
+          win_load8(w0, x);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float sc = __fadd_rn(c.cum, __fsub_rn(x[i], lse));
-            p[i] = (i0 + i < deg) && (sc >= thr_s || c.lo_tok + i0 + i == P.eos);
+            p[i] = (i0 + i >= 0) && (i0 + i < deg) && (sc >= thr_s || c.lo_tok + i0 + i == P.eos);
             any |= p[i];
           }
         } else {
@@ -491,7 +493,7 @@ struct Step {
           }
         }
         csync();
-        if (base + kBatch < deg && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
+        if (base + kBatch < d0 + deg && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
           const Cut cut = shrink_to(P.k2);
           raise_tau(c.r, cut.floor_key());
         }
@@ -882,8 +884,8 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
       const int lo = max(lt - P.voff, 0);
       const int hi = min(ht - P.voff, P.VL - 1);
       if (lo <= hi) {
-        c.wlo = lo;
-        c.whi = min(hi, lo + Step<TL>::kWinTok - 1);
+        c.wlo = lo & ~7;                 // window index 0 = an 8-aligned column
+        c.whi = min(hi, c.wlo + Step<TL>::kWinTok - 1);
       }
     }
     c.cum = P.cum[c.row];
@@ -944,6 +946,8 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
     float thr_y = -kInf;
     uint64_t thr_key = 0ull;
     const Geom g = row_geom<ES>(P, c.row);
+    // whole-vector window copies need vectors that start on window-vector boundaries
+    const bool win_vec_ok = (g.head % EPV) == 0;
     // fast-path scale: exp(y - m) = 2^(x * a - m * log2e) with y = x (raw) or x / T
     const float a = kLog2e * ((P.mode == kModeProcessed) ? c.rteff : 1.0f);
     uint64_t sacc0 = pack2(0.0f, 0.0f), sacc1 = pack2(0.0f, 0.0f);
@@ -977,7 +981,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
       const uint4* sv = reinterpret_cast<const uint4*>(S.ring + static_cast<size_t>(cstage) * kStageBytes);
       const int tbase = g.head + ch * kChunkElems;
       const bool in_window = c.constrained && tbase + kChunkElems > c.wlo && tbase <= c.whi;
-      if (fast_ok && !in_window) {
+      if (fast_ok && (!in_window || win_vec_ok)) {
         // fast path: kVecPerThread 16-byte vectors per thread, packed f32x2 math
         constexpr int kVecPerThread = kChunkVecs / kThreads;
         static_assert(kChunkVecs % kThreads == 0, "whole vectors per thread per stage");
@@ -985,6 +989,29 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
 #pragma unroll
         for (int j = 0; j < kVecPerThread; ++j)
           vv[j] = (tid + j * kThreads < nvec) ? sv[tid + j * kThreads] : make_uint4(0, 0, 0, 0);
+        if (in_window) {
+          // keep the raw vectors that fall in the row's child window (vector aligned)
+          uint4* wv = reinterpret_cast<uint4*>(S.win);
+#pragma unroll
+          for (int j = 0; j < kVecPerThread; ++j) {
+            const int tb = tbase + (tid + j * kThreads) * EPV;
+            if (tid + j * kThreads < nvec && tb + EPV > c.wlo && tb <= c.whi) wv[(tb - c.wlo) / EPV] = vv[j];
+          }
+        }
+        if (m == -kInf) {
+          // seed the running reference with this thread's own maximum (any element works)
+          float mx = -kInf;
+#pragma unroll
+          for (int j = 0; j < kVecPerThread; ++j) {
+            if (tid + j * kThreads < nvec) {
+              float x[EPV];
+              Tr::unpack(vv[j], x);
+#pragma unroll
+              for (int i = 0; i < EPV; ++i) mx = fmaxf(mx, x[i]);
+            }
+          }
+          m = (P.mode == kModeProcessed) ? mx * c.rteff : mx;
+        }
         const float cm = -m * kLog2e;
         const uint64_t A2 = pack2(a, a), C2 = pack2(cm, cm);
         uint64_t p0 = pack2(0.0f, 0.0f), p1 = pack2(0.0f, 0.0f);
