@@ -293,7 +293,7 @@ def run_ours(args):
                      "algorithmic_bytes_per_launch": int(np.mean(steps_bytes)),
                      "avg_launch_ms": round(avg_launch_ms, 5), "per_level_ms": per_level_ms,
                      "per_level_bytes": [int(b) for b in bytes_cycle]},
-        "gpu_launches": 2 * args.steps,          # fused_step_kernel + merge_kernel per step
+        "gpu_launches": 3 * args.steps,          # row_meta_kernel + fused_step_kernel + merge_kernel per step
         "clocks": clk,
         "device_errors": err,
     }

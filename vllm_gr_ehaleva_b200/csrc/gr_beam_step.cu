@@ -79,6 +79,7 @@ struct Params {
   // workspace
   unsigned long long* tau;     // [R] running lower bound of the request's 2B-th key
   unsigned int* rowcnt;        // [R*NB] keys in each row's slot
+  int* meta;                   // [R*NB][kMetaWords] row metadata resolved by row_meta_kernel
   unsigned long long* buf;     // [R*NB][2B] per-row candidate slots
   // derived
   int k2;        // 2B candidates
@@ -93,7 +94,15 @@ struct Params {
 // Shared-memory layout (dynamic shared memory).  Every piece but the ring sits
 // at a compile-time offset, so accesses need no pointer arithmetic at run time;
 // the optional penalty pieces follow, and the ring of bulk-copy stages is last.
+// Row metadata record (kMetaWords 32-bit words), resolved for every row by
+// row_meta_kernel before the fused kernel so that a row's setup is one
+// prefetched load instead of a chain of dependent loads.
+constexpr int kMetaSmall = 16;                  // child tokens kept for small nodes
+constexpr int kMetaWords = 8 + kMetaSmall;      // 96 bytes
+enum MetaWord { kMNode = 0, kMCum = 1, kMC0 = 2, kMC1 = 3, kMLo = 4, kMHi = 5, kMToks = 8 };
+
 struct Scalars {
+  int meta[kMetaWords];        // the current row's record
   uint32_t cnt;
   uint32_t ntab;
   int overflow;
@@ -509,7 +518,9 @@ struct Step {
 #pragma unroll
         for (int i = 0; i < kPer; ++i) {
           const int j = base + i * kThreads + static_cast<int>(threadIdx.x);
-          toks[i] = (j >= end) ? -1 : (c.dense ? c.lo_tok + (j - c0) : __ldg(P.child_tok + j));
+          toks[i] = (j >= end) ? -1
+                  : (c.dense ? c.lo_tok + (j - c0)
+                             : (deg <= kMetaSmall ? S.v->meta[kMToks + (j - c0)] : __ldg(P.child_tok + j)));
         }
         float xs[kPer];
         bool p[kPer];
@@ -816,6 +827,38 @@ done:
   S.v->producer_done = 1;
 }
 
+// One thread per row: node -> CSR range -> child-token bounds (and, for small
+// nodes, every child token).
+__global__ void __launch_bounds__(256) row_meta_kernel(const __grid_constant__ Params P) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= P.R * P.NB) return;
+  int w[kMetaWords];
+#pragma unroll
+  for (int i = 0; i < kMetaWords; ++i) w[i] = 0;
+  int node = P.node[row];
+  if (node < GR_NODE_DEAD || node >= P.N) {
+    atomicOr(P.err, GR_DEVERR_BAD_NODE);
+    node = GR_NODE_DEAD;
+  }
+  w[kMNode] = node;
+  w[kMCum] = __float_as_int(P.cum[row]);
+  if (node >= 0) {
+    const int c0 = static_cast<int>(P.row_ptr[node]);
+    const int c1 = static_cast<int>(P.row_ptr[node + 1]);
+    w[kMC0] = c0;
+    w[kMC1] = c1;
+    if (c1 > c0) {
+      w[kMLo] = P.child_tok[c0];
+      w[kMHi] = P.child_tok[c1 - 1];
+      if (c1 - c0 <= kMetaSmall)
+        for (int j = 0; j < c1 - c0; ++j) w[kMToks + j] = P.child_tok[c0 + j];
+    }
+  }
+  int4* dst = reinterpret_cast<int4*>(P.meta + static_cast<size_t>(row) * kMetaWords);
+#pragma unroll
+  for (int i = 0; i < kMetaWords / 4; ++i) dst[i] = make_int4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+}
+
 template <typename TL>
 __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_constant__ Params P) {
   const Smem S = smem_view(P);
@@ -853,6 +896,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
   int cstage = 0;
   uint32_t cphase = 0;
   long long consumed = 0;
+  int meta_word = 0;                 // word tid (< kMetaWords) of the next row's metadata record
   GR_PROF_T(t_kernel);
   for (int it = 0; it < my_n; ++it) {
     // ------------------------------------------------------------ row setup
@@ -861,24 +905,23 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
     c.row = row_of_iter(P, it);
     c.r = c.row / P.NB;
     c.b = c.row - c.r * P.NB;
-    c.node = P.node[c.row];
-    if (c.node < GR_NODE_DEAD || c.node >= P.N) {
-      if (tid == 0) atomicOr(P.err, GR_DEVERR_BAD_NODE);
-      c.node = GR_NODE_DEAD;
-    }
+    // the row's metadata record: word tid was prefetched during the previous row
+    if (it == 0 && tid < kMetaWords) meta_word = __ldcg(P.meta + static_cast<size_t>(c.row) * kMetaWords + tid);
+    if (tid < kMetaWords) S.v->meta[tid] = meta_word;
+    csync();
+    if (tid < kMetaWords && it + 1 < my_n)
+      meta_word = __ldcg(P.meta + static_cast<size_t>(row_of_iter(P, it + 1)) * kMetaWords + tid);
+    c.node = S.v->meta[kMNode];
     c.stream = (P.K > 0) || (c.node == GR_NODE_UNCONSTRAINED);
     c.constrained = !c.stream && c.node >= 0;
-    c.c0 = c.c1 = 0;
-    if (c.node >= 0) {
-      c.c0 = static_cast<int>(P.row_ptr[c.node]);
-      c.c1 = static_cast<int>(P.row_ptr[c.node + 1]);
-    }
+    c.c0 = S.v->meta[kMC0];
+    c.c1 = S.v->meta[kMC1];
     c.wlo = 1;
     c.whi = 0;
     c.lo_tok = 0;
     c.dense = false;
     if (c.constrained && c.c1 > c.c0) {
-      const int lt = P.child_tok[c.c0], ht = P.child_tok[c.c1 - 1];
+      const int lt = S.v->meta[kMLo], ht = S.v->meta[kMHi];
       c.lo_tok = lt;
       c.dense = (ht - lt + 1) == (c.c1 - c.c0);
       const int lo = max(lt - P.voff, 0);
@@ -888,7 +931,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
         c.whi = min(hi, c.wlo + Step<TL>::kWinTok - 1);
       }
     }
-    c.cum = P.cum[c.row];
+    c.cum = __int_as_float(S.v->meta[kMCum]);
     c.teff = (P.mode == kModeProcessed) ? eff_temperature(P, c.r) : 1.0f;
     c.rteff = __frcp_rn(c.teff);
     c.rep = P.rep ? P.rep[c.r] : 1.0f;
@@ -1427,9 +1470,11 @@ static int device_info(DeviceInfo** out) {
   return GR_OK;
 }
 
-// Workspace: tau [R] u64 | row counts [R*NB] u32 | row slots [R*NB][2B] u64.
+// Workspace: tau [R] u64 | row counts [R*NB] u32 | row metadata [R*NB][kMetaWords] i32 |
+// row slots [R*NB][2B] u64.
 static size_t ws_tau_bytes(int R) { return align128(size_t(R) * 8); }
 static size_t ws_cnt_bytes(int R, int NB) { return align128(size_t(R) * NB * 4); }
+static size_t ws_meta_bytes(int R, int NB) { return align128(size_t(R) * NB * kMetaWords * 4); }
 
 static int validate(const gr_step_desc* d) {
   if (!d) return GR_ERR_NULL;
@@ -1599,7 +1644,8 @@ int32_t gr_beam_step_workspace_size(const gr_step_desc* d, size_t* bytes) {
   const int v = validate(d);
   if (v != GR_OK) return v;
   const size_t slots = size_t(d->num_requests) * d->num_beams * size_t(2 * d->beam_width);
-  *bytes = ws_tau_bytes(d->num_requests) + ws_cnt_bytes(d->num_requests, d->num_beams) + align128(slots * 8);
+  *bytes = ws_tau_bytes(d->num_requests) + ws_cnt_bytes(d->num_requests, d->num_beams) +
+           ws_meta_bytes(d->num_requests, d->num_beams) + align128(slots * 8);
   return GR_OK;
 }
 
@@ -1631,9 +1677,16 @@ int32_t gr_beam_step(const gr_step_desc* d, const gr_step_io* io, void* workspac
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   P.tau = reinterpret_cast<unsigned long long*>(ws);
   P.rowcnt = reinterpret_cast<unsigned int*>(ws + ws_tau_bytes(R));
-  P.buf = reinterpret_cast<unsigned long long*>(ws + ws_tau_bytes(R) + ws_cnt_bytes(R, d->num_beams));
+  P.meta = reinterpret_cast<int*>(ws + ws_tau_bytes(R) + ws_cnt_bytes(R, d->num_beams));
+  P.buf = reinterpret_cast<unsigned long long*>(ws + ws_tau_bytes(R) + ws_cnt_bytes(R, d->num_beams) +
+                                                ws_meta_bytes(R, d->num_beams));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(ws, 0, size_t(R) * 8, s) != cudaSuccess) return GR_ERR_CUDA;
+  {
+    const int rows = R * d->num_beams;
+    row_meta_kernel<<<(rows + 255) / 256, 256, 0, s>>>(P);
+    if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
+  }
   v = launch_by_dtype(P, d->logit_dtype, dev, s);
   if (v != GR_OK) return v;
   return launch_merge(P, dev, s);
