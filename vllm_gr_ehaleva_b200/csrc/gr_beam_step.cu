@@ -711,16 +711,21 @@ struct Step {
 
   // Write the row's keys that beat the request threshold into the row's own
   // slot of the candidate buffer (no atomics; the merge kernel gathers them).
-  __device__ void emit(const RowCtx& c) {
+  __device__ void emit(const RowCtx& c, bool refilter) {
     const Smem S = smem_view(P);
-    if (threadIdx.x == 0) {
-      const uint64_t t = S.v->tau_pref;       // read at row start; a stale bound is still valid
-      if (t > S.v->thr_key) S.v->thr_key = t;
+    int n;
+    if (refilter) {
+      if (threadIdx.x == 0) {
+        const uint64_t t = S.v->tau_pref;       // read at row start; a stale bound is still valid
+        if (t > S.v->thr_key) S.v->thr_key = t;
+      }
+      csync();
+      const uint64_t thr = S.v->thr_key;
+      n = min(static_cast<int>(S.v->cnt), kKeyCap);
+      if (thr > 0 && n > 0) n = static_cast<int>(cta_compact(S.keys, n, Cut{thr, 0}, &S.v->cnt));
+    } else {
+      n = min(static_cast<int>(S.v->cnt), kKeyCap);
     }
-    csync();
-    const uint64_t thr = S.v->thr_key;
-    int n = min(static_cast<int>(S.v->cnt), kKeyCap);
-    if (thr > 0 && n > 0) n = static_cast<int>(cta_compact(S.keys, n, Cut{thr, 0}, &S.v->cnt));
     if (n > P.k2) {                     // cannot happen: every path selects at most 2B
       if (threadIdx.x == 0) atomicOr(P.err, GR_DEVERR_OVERFLOW);
       n = P.k2;
@@ -1181,30 +1186,34 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
       S.red_m[warp] = m;
       S.red_s[warp] = s;
     }
-    csync();
-    if (tid == 0) {
-      float M = -kInf;
-      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, S.red_m[w]);
-      float tot = 0.0f;
-      if (M > -kInf)
-        for (int w = 0; w < kWarps; ++w) tot += S.red_s[w] * fast_exp2((S.red_m[w] - M) * kLog2e);
-      S.v->m_tot = M;
-      S.v->s_tot = tot;
-      S.v->lse = M + logf(tot);
-      if (P.lse_out) P.lse_out[c.row] = S.v->lse;
-      if (P.partial_only) P.partials[c.row] = make_float2(M, tot);
+    if (tid == 0 && !P.partial_only) {
+      S.v->tau_pref = tau_pref;
+      if (c.constrained) S.v->thr_key = tau_pref;      // candidates start from the request bound
     }
     csync();
+    // every thread combines the warp partials (same order, same result everywhere)
+    float lse;
+    {
+      float M = -kInf;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, S.red_m[w]);
+      float tot = 0.0f;
+      if (M > -kInf) {
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) tot += S.red_s[w] * fast_exp2((S.red_m[w] - M) * kLog2e);
+      }
+      lse = M + logf(tot);
+      if (tid == 0) {
+        if (P.lse_out) P.lse_out[c.row] = lse;
+        if (P.partial_only) P.partials[c.row] = make_float2(M, tot);
+      }
+    }
     GR_PROF_ADD(2, t_red);
     if (S.v->abort) goto drain;
-    const float lse = S.v->lse;
     GR_PROF_T(t_cand);
 
     if (!P.partial_only) {
-      if (tid == 0) S.v->tau_pref = tau_pref;
       if (c.constrained) {
-        if (tid == 0) S.v->thr_key = tau_pref;
-        csync();
         st.constrained_candidates(c, lse);
       } else if (c.stream && P.K == 0) {
         st.unconstrained_candidates(c, lse);
@@ -1219,7 +1228,8 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
         if (tid == 0) S.v->thr_key = 0ull;
         csync();
       }
-      st.emit(c);
+      // constrained rows were filtered against the request bound while they were scored
+      st.emit(c, /*refilter=*/!c.constrained);
       GR_PROF_ADD(4, t_emit);
     }
     if (c.pen_active) {
