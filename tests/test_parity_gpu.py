@@ -18,6 +18,14 @@ from vllm_gr_ehaleva_b200.synthetic import histories, initial_cum
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True, params=["auto", "stream"])
+def step_kernel(request, monkeypatch):
+    """Run every case through both step kernels: the automatic choice (the
+    warp-specialised kernel where a step qualifies) and the streaming kernel."""
+    monkeypatch.setenv("GR_BEAM_KERNEL", request.param)
+    return request.param
+
+
 def _constrained_case(dtype, R=3, NB=16, B=16, V=8192, seed=0, sigma=4.0, row_pad=0):
     cat = small_catalog(V=V)
     node = np.full((R, NB), cat.start_node, np.int32)
@@ -165,3 +173,22 @@ def test_full_vocab_cfg2_rows():
         gpu = gpu_step(case)
         assert_step_parity(case, gpu)
         case = next_inputs(case, gpu, make_logits(R, NB, V, 4.0, 50 + step, "bf16"))
+
+
+def test_mixed_rows_many_per_cta():
+    # several rows per CTA (the warp-specialised kernel's two row slots cycle),
+    # constrained rows at two catalog depths, rows without a node (re-read by
+    # the row-end warps) and dead rows in one step
+    cat = small_catalog(V=32768)
+    R, NB, B, V = 8, 128, 32, 32768
+    rng = np.random.default_rng(12)
+    kinds = rng.integers(0, 10, size=(R, NB))
+    first = cat.csr.child_node[cat.csr.row_ptr[cat.start_node]:cat.csr.row_ptr[cat.start_node + 1]]
+    node = np.full((R, NB), cat.start_node, np.int32)
+    deep = kinds >= 7
+    node[deep] = first[rng.integers(0, len(first), size=int(deep.sum()))]   # one level down
+    node[kinds == 0] = -1                      # unconstrained
+    node[kinds == 1] = -2                      # dead
+    case = Case(logits32=make_logits(R, NB, V, 4.0, 77, "bf16"), dtype="bf16", cum=initial_cum(R, NB),
+                node=node, beam_width=B, vocab_size=V, csr=cat.csr)
+    assert_step_parity(case, gpu_step(case))

@@ -20,6 +20,8 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <cuda_runtime.h>
 #include <mutex>
 #include <type_traits>
@@ -32,19 +34,26 @@ namespace gr {
 constexpr int kModeProcessed = 1;
 
 // Optional per-phase cycle counters (compile with -DGR_PHASE_PROFILE; off in
-// the product build).  Thread 0 of every CTA adds clock64 deltas per phase.
+// the product build).  Thread 0 of every CTA adds clock64 deltas per phase
+// into shared memory and flushes them to g_phase when the CTA ends.
 #ifdef GR_PHASE_PROFILE
 constexpr int kProfSlots = 16;
 __device__ unsigned long long g_phase[1024][kProfSlots];
 #define GR_PROF_T(var) const long long var = clock64()
 #define GR_PROF_ADD(slot, t0) \
-  do { if (threadIdx.x == 0) g_phase[blockIdx.x][slot] += clock64() - (t0); } while (0)
+  do { if (threadIdx.x == 0) S.v->prof[slot] += clock64() - (t0); } while (0)
 #define GR_PROF_CNT(slot) \
-  do { if (threadIdx.x == 0) g_phase[blockIdx.x][slot] += 1; } while (0)
+  do { if (threadIdx.x == 0) S.v->prof[slot] += 1; } while (0)
+#define GR_PROF_INIT() \
+  do { if (threadIdx.x < kProfSlots) S.v->prof[threadIdx.x] = 0; } while (0)
+#define GR_PROF_FLUSH() \
+  do { if (threadIdx.x == 0) for (int q = 0; q < kProfSlots; ++q) g_phase[blockIdx.x][q] += S.v->prof[q]; } while (0)
 #else
 #define GR_PROF_T(var)
 #define GR_PROF_ADD(slot, t0) do { } while (0)
 #define GR_PROF_CNT(slot) do { } while (0)
+#define GR_PROF_INIT() do { } while (0)
+#define GR_PROF_FLUSH() do { } while (0)
 #endif
 
 struct Params {
@@ -99,7 +108,7 @@ struct Params {
 // prefetched load instead of a chain of dependent loads.
 constexpr int kMetaSmall = 16;                  // child tokens kept for small nodes
 constexpr int kMetaWords = 8 + kMetaSmall;      // 96 bytes
-enum MetaWord { kMNode = 0, kMCum = 1, kMC0 = 2, kMC1 = 3, kMLo = 4, kMHi = 5, kMToks = 8 };
+enum MetaWord { kMNode = 0, kMCum = 1, kMC0 = 2, kMC1 = 3, kMLo = 4, kMHi = 5, kMTeff = 6, kMToks = 8 };
 
 struct Scalars {
   int meta[kMetaWords];        // the current row's record
@@ -119,6 +128,9 @@ struct Scalars {
   uint64_t tau_pref;
   long long issued;
   int producer_done;
+#ifdef GR_PHASE_PROFILE
+  unsigned long long prof[kProfSlots];
+#endif
 };
 
 __host__ __device__ constexpr size_t align128(size_t x) { return (x + 127) & ~size_t(127); }
@@ -188,7 +200,7 @@ struct Geom {
   int nchunks;
 };
 
-template <int ES>
+template <int ES, int SB = kStageBytes>
 __device__ __forceinline__ Geom row_geom(const Params& P, int row) {
   Geom g;
   g.rowp = static_cast<const char*>(P.logits) + static_cast<size_t>(row) * static_cast<size_t>(P.row_stride) * ES;
@@ -207,7 +219,7 @@ __device__ __forceinline__ Geom row_geom(const Params& P, int row) {
     g.body_bytes = static_cast<long long>(a1 - a0);
     g.head = static_cast<int>((a0 - a) / ES);
     g.tail_start = static_cast<int>((a1 - a) / ES);
-    g.nchunks = static_cast<int>((g.body_bytes + kStageBytes - 1) / kStageBytes);
+    g.nchunks = static_cast<int>((g.body_bytes + SB - 1) / SB);
   }
   return g;
 }
@@ -259,6 +271,8 @@ struct Step {
   static constexpr int EPV = Tr::kPerVec;
 
   const Params& P;
+  int win_off = 0;            // byte offset of the current row's window from the first window
+  const int* rec = nullptr;   // the current row's metadata record (shared memory)
   __device__ __forceinline__ explicit Step(const Params& p) : P(p) {}
 
   __device__ __forceinline__ float load_logit(const RowCtx& c, int tl) const {
@@ -269,24 +283,23 @@ struct Step {
 
   static constexpr int kWinTok = kWinBytes / ES;
 
+  __device__ __forceinline__ unsigned char* win() const { return g_smem + kOffWin + win_off; }
   __device__ __forceinline__ void win_store(int i, float x) const {
-    const Smem S = smem_view(P);
     if constexpr (ES == 4) {
-      reinterpret_cast<float*>(S.win)[i] = x;
+      reinterpret_cast<float*>(win())[i] = x;
     } else if constexpr (std::is_same_v<TL, __nv_bfloat16>) {
-      reinterpret_cast<unsigned short*>(S.win)[i] = static_cast<unsigned short>(__float_as_uint(x) >> 16);
+      reinterpret_cast<unsigned short*>(win())[i] = static_cast<unsigned short>(__float_as_uint(x) >> 16);
     } else {
-      reinterpret_cast<__half*>(S.win)[i] = __float2half_rn(x);
+      reinterpret_cast<__half*>(win())[i] = __float2half_rn(x);
     }
   }
   __device__ __forceinline__ float win_load(int i) const {
-    const Smem S = smem_view(P);
     if constexpr (ES == 4) {
-      return reinterpret_cast<const float*>(S.win)[i];
+      return reinterpret_cast<const float*>(win())[i];
     } else if constexpr (std::is_same_v<TL, __nv_bfloat16>) {
-      return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const unsigned short*>(S.win)[i]) << 16);
+      return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const unsigned short*>(win())[i]) << 16);
     } else {
-      return __half2float(reinterpret_cast<const __half*>(S.win)[i]);
+      return __half2float(reinterpret_cast<const __half*>(win())[i]);
     }
   }
 
@@ -432,14 +445,13 @@ struct Step {
   // ---- row-end candidate formation -----------------------------------------
   // Load window entries [i, i+8) (i a multiple of 8) as floats.
   __device__ __forceinline__ void win_load8(int i, float* x) const {
-    const Smem S = smem_view(P);
     if constexpr (ES == 4) {
-      const uint4 a = reinterpret_cast<const uint4*>(S.win)[i >> 2];
-      const uint4 b = reinterpret_cast<const uint4*>(S.win)[(i >> 2) + 1];
+      const uint4 a = reinterpret_cast<const uint4*>(win())[i >> 2];
+      const uint4 b = reinterpret_cast<const uint4*>(win())[(i >> 2) + 1];
       x[0] = __uint_as_float(a.x); x[1] = __uint_as_float(a.y); x[2] = __uint_as_float(a.z); x[3] = __uint_as_float(a.w);
       x[4] = __uint_as_float(b.x); x[5] = __uint_as_float(b.y); x[6] = __uint_as_float(b.z); x[7] = __uint_as_float(b.w);
     } else {
-      Tr::unpack(reinterpret_cast<const uint4*>(S.win)[i >> 3], x);
+      Tr::unpack(reinterpret_cast<const uint4*>(win())[i >> 3], x);
     }
   }
 
@@ -520,7 +532,7 @@ struct Step {
           const int j = base + i * kThreads + static_cast<int>(threadIdx.x);
           toks[i] = (j >= end) ? -1
                   : (c.dense ? c.lo_tok + (j - c0)
-                             : (deg <= kMetaSmall ? S.v->meta[kMToks + (j - c0)] : __ldg(P.child_tok + j)));
+                             : (deg <= kMetaSmall ? rec[kMToks + (j - c0)] : __ldg(P.child_tok + j)));
         }
         float xs[kPer];
         bool p[kPer];
@@ -736,6 +748,47 @@ struct Step {
   }
 };
 
+// Row context from the row's metadata record (c.row, c.r, c.b already set).
+template <typename TL>
+__device__ __forceinline__ void fill_row_ctx(const Params& P, const int* rec, RowCtx& c) {
+  c.node = rec[kMNode];
+  c.stream = (P.K > 0) || (c.node == GR_NODE_UNCONSTRAINED);
+  c.constrained = !c.stream && c.node >= 0;
+  c.c0 = rec[kMC0];
+  c.c1 = rec[kMC1];
+  c.wlo = 1;
+  c.whi = 0;
+  c.lo_tok = 0;
+  c.dense = false;
+  if (c.constrained && c.c1 > c.c0) {
+    const int lt = rec[kMLo], ht = rec[kMHi];
+    c.lo_tok = lt;
+    c.dense = (ht - lt + 1) == (c.c1 - c.c0);
+    const int lo = max(lt - P.voff, 0);
+    const int hi = min(ht - P.voff, P.VL - 1);
+    if (lo <= hi) {
+      c.wlo = lo & ~7;                 // window index 0 = an 8-aligned column
+      c.whi = min(hi, c.wlo + Step<TL>::kWinTok - 1);
+    }
+  }
+  c.cum = __int_as_float(rec[kMCum]);
+  c.teff = __int_as_float(rec[kMTeff]);
+  c.rteff = __frcp_rn(c.teff);
+  // penalties matter for processed log-probs and for the per-beam top-K's greedy token
+  const bool pen_used = P.pen && P.T > 0 &&
+                        (P.partial_only ? P.mode == kModeProcessed : (P.mode == kModeProcessed || P.K > 0));
+  c.rep = (pen_used && P.rep) ? P.rep[c.r] : 1.0f;
+  c.pres = (pen_used && P.pres) ? P.pres[c.r] : 0.0f;
+  c.freq = (pen_used && P.freq) ? P.freq[c.r] : 0.0f;
+  c.pen_active = pen_used && !(c.rep == 1.0f && c.pres == 0.0f && c.freq == 0.0f);
+  if (P.partial_only) {
+    // vocab-sharded phase 1: only the normaliser of the local columns
+    c.stream = false;
+    c.constrained = false;
+  }
+  c.excl = c.pen_active && P.mode == kModeProcessed;
+}
+
 // Add the fast-path accumulators (relative to the same reference max) into s.
 __device__ __forceinline__ void fold(uint64_t& a0, uint64_t& a1, float& s) {
   float q0, q1, q2, q3;
@@ -794,16 +847,17 @@ struct FastSum<float> {
   }
 };
 
-// Producer warp, lane 0: fill the ring with the CTA's (row, chunk) sequence.
-template <int ES>
-__device__ __forceinline__ void produce(const Params& P, int my_n) {
+// Producer warp, lane 0: fill the ring (stages of SB bytes at `ring`) with the
+// CTA's (row, chunk) sequence.
+template <int ES, int SB = kStageBytes>
+__device__ __forceinline__ void produce(const Params& P, int my_n, unsigned char* ring) {
   const Smem S = smem_view(P);
   const uint64_t pol = l2_policy_evict_first();
   int stage = 0;
   uint32_t round = 0;
   long long fills = 0;
   for (int it = 0; it < my_n; ++it) {
-    const Geom g = row_geom<ES>(P, row_of_iter(P, it));
+    const Geom g = row_geom<ES, SB>(P, row_of_iter(P, it));
     for (int ch = 0; ch < g.nchunks; ++ch) {
       if (fills >= P.stages) {
         if (!mbar_wait_bounded(&S.empty[stage], (round - 1u) & 1u, &S.v->abort)) {
@@ -813,11 +867,11 @@ __device__ __forceinline__ void produce(const Params& P, int my_n) {
         }
       }
       {
-        const long long off = static_cast<long long>(ch) * kStageBytes;
-        const uint32_t bytes = static_cast<uint32_t>(min(static_cast<long long>(kStageBytes), g.body_bytes - off));
+        const long long off = static_cast<long long>(ch) * SB;
+        const uint32_t bytes = static_cast<uint32_t>(min(static_cast<long long>(SB), g.body_bytes - off));
         fence_proxy_async_smem();
         mbar_arrive_expect_tx(&S.full[stage], bytes);
-        bulk_copy_g2s(S.ring + static_cast<size_t>(stage) * kStageBytes, g.body + off, bytes, &S.full[stage], pol);
+        bulk_copy_g2s(ring + static_cast<size_t>(stage) * SB, g.body + off, bytes, &S.full[stage], pol);
       }
       ++fills;
       if (++stage == P.stages) {
@@ -847,6 +901,7 @@ __global__ void __launch_bounds__(256) row_meta_kernel(const __grid_constant__ P
   }
   w[kMNode] = node;
   w[kMCum] = __float_as_int(P.cum[row]);
+  w[kMTeff] = __float_as_int((P.mode == kModeProcessed) ? eff_temperature(P, row / P.NB) : 1.0f);
   if (node >= 0) {
     const int c0 = static_cast<int>(P.row_ptr[node]);
     const int c1 = static_cast<int>(P.row_ptr[node + 1]);
@@ -891,10 +946,11 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
   }
   if (P.pen)
     for (int i = tid; i < P.bm_words; i += kBlock) S.bitmap[i] = 0u;
+  GR_PROF_INIT();
   __syncthreads();   // the only CTA-wide barrier: consumers use csync() from here on
 
   if (warp == kWarps) {
-    if (lane == 0) produce<ES>(P, my_n);
+    if (lane == 0) produce<ES>(P, my_n, S.ring);
     return;
   }
 
@@ -906,6 +962,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
   for (int it = 0; it < my_n; ++it) {
     // ------------------------------------------------------------ row setup
     GR_PROF_CNT(10);
+    GR_PROF_T(t_row);
     RowCtx c;
     c.row = row_of_iter(P, it);
     c.r = c.row / P.NB;
@@ -916,42 +973,8 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
     csync();
     if (tid < kMetaWords && it + 1 < my_n)
       meta_word = __ldcg(P.meta + static_cast<size_t>(row_of_iter(P, it + 1)) * kMetaWords + tid);
-    c.node = S.v->meta[kMNode];
-    c.stream = (P.K > 0) || (c.node == GR_NODE_UNCONSTRAINED);
-    c.constrained = !c.stream && c.node >= 0;
-    c.c0 = S.v->meta[kMC0];
-    c.c1 = S.v->meta[kMC1];
-    c.wlo = 1;
-    c.whi = 0;
-    c.lo_tok = 0;
-    c.dense = false;
-    if (c.constrained && c.c1 > c.c0) {
-      const int lt = S.v->meta[kMLo], ht = S.v->meta[kMHi];
-      c.lo_tok = lt;
-      c.dense = (ht - lt + 1) == (c.c1 - c.c0);
-      const int lo = max(lt - P.voff, 0);
-      const int hi = min(ht - P.voff, P.VL - 1);
-      if (lo <= hi) {
-        c.wlo = lo & ~7;                 // window index 0 = an 8-aligned column
-        c.whi = min(hi, c.wlo + Step<TL>::kWinTok - 1);
-      }
-    }
-    c.cum = __int_as_float(S.v->meta[kMCum]);
-    c.teff = (P.mode == kModeProcessed) ? eff_temperature(P, c.r) : 1.0f;
-    c.rteff = __frcp_rn(c.teff);
-    c.rep = P.rep ? P.rep[c.r] : 1.0f;
-    c.pres = P.pres ? P.pres[c.r] : 0.0f;
-    c.freq = P.freq ? P.freq[c.r] : 0.0f;
-    const bool has_pen = P.pen && P.T > 0 && !(c.rep == 1.0f && c.pres == 0.0f && c.freq == 0.0f);
-    if (P.partial_only) {
-      // vocab-sharded phase 1: only the normaliser of the local columns
-      c.stream = false;
-      c.constrained = false;
-      c.pen_active = has_pen && P.mode == kModeProcessed;
-    } else {
-      c.pen_active = has_pen && (P.mode == kModeProcessed || P.K > 0);
-    }
-    c.excl = c.pen_active && P.mode == kModeProcessed;
+    fill_row_ctx<TL>(P, S.v->meta, c);
+    st.rec = S.v->meta;
     const bool fast_ok = !c.stream && !c.excl;
 
     if (tid == 0) {
@@ -1015,6 +1038,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
     }
 
     // ------------------------------------------------------------ body chunks
+    GR_PROF_ADD(5, t_row);
     GR_PROF_T(t_stream);
     for (int ch = 0; ch < g.nchunks; ++ch) {
       GR_PROF_T(t_wait);
@@ -1039,7 +1063,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
           vv[j] = (tid + j * kThreads < nvec) ? sv[tid + j * kThreads] : make_uint4(0, 0, 0, 0);
         if (in_window) {
           // keep the raw vectors that fall in the row's child window (vector aligned)
-          uint4* wv = reinterpret_cast<uint4*>(S.win);
+          uint4* wv = reinterpret_cast<uint4*>(st.win());
 #pragma unroll
           for (int j = 0; j < kVecPerThread; ++j) {
             const int tb = tbase + (tid + j * kThreads) * EPV;
@@ -1239,6 +1263,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
     csync();
   }
   GR_PROF_ADD(11, t_kernel);
+  GR_PROF_FLUSH();
   return;
 
 drain:
@@ -1260,6 +1285,8 @@ drain:
   }
   csync();
 }
+
+#include "gr_step_ws.cuh"
 
 // ---------------------------------------------------------------- merge kernel
 // One CTA of kThreads threads per request: gathers the request's per-row
@@ -1449,6 +1476,7 @@ struct DeviceInfo {
   int smem_reserved = 0;
   int major = 0;
   bool attr_set[3] = {false, false, false};
+  bool ws_attr_set[3] = {false, false, false};
   bool merge_attr_set = false;
 };
 
@@ -1603,6 +1631,53 @@ static int launch_fused(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream_t 
   return GR_OK;
 }
 
+// The warp-specialised kernel takes steps whose rows need no streamed
+// selection and no penalty exclusion.  GR_BEAM_KERNEL=stream|ws forces one
+// kernel (ws only where eligible); anything else selects automatically.
+static bool ws_eligible(const Params& P) {
+  return P.K == 0 && !P.partial_only && !(P.mode == kModeProcessed && P.pen && P.T > 0);
+}
+
+static int kernel_choice() {
+  const char* e = std::getenv("GR_BEAM_KERNEL");
+  if (e == nullptr) return 0;
+  if (std::strcmp(e, "stream") == 0) return 1;
+  if (std::strcmp(e, "ws") == 0) return 2;
+  return 0;
+}
+
+template <typename TL>
+static int launch_fused_ws(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream_t stream) {
+  int stages = 0;
+  for (int st = ws::kMaxStagesWs; st >= 3; --st) {
+    if (ws::smem_bytes(st) <= static_cast<size_t>(dev->smem_optin)) {
+      stages = st;
+      break;
+    }
+  }
+  if (stages == 0) return launch_fused<TL>(P, dev, dtype_idx, stream);
+  P.stages = stages;
+  const size_t smem = ws::smem_bytes(stages);
+  if (!dev->ws_attr_set[dtype_idx]) {
+    if (cudaFuncSetAttribute(fused_step_ws_kernel<TL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             dev->smem_optin) != cudaSuccess)
+      return GR_ERR_CUDA;
+    dev->ws_attr_set[dtype_idx] = true;
+  }
+  const int total = P.R * P.NB;
+  const int grid = total < dev->sms ? total : dev->sms;
+  fused_step_ws_kernel<TL><<<grid, ws::kBlockWs, smem, stream>>>(P);
+  if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
+  return GR_OK;
+}
+
+template <typename TL>
+static int launch_step_kernel(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream_t stream) {
+  const int choice = kernel_choice();
+  if (choice != 1 && ws_eligible(P)) return launch_fused_ws<TL>(P, dev, dtype_idx, stream);
+  return launch_fused<TL>(P, dev, dtype_idx, stream);
+}
+
 static int launch_merge(const Params& P, DeviceInfo* dev, cudaStream_t stream) {
   const size_t smem = merge_smem_bytes(P.NB);
   if (smem > static_cast<size_t>(dev->smem_optin)) return GR_ERR_UNSUPPORTED;
@@ -1619,9 +1694,9 @@ static int launch_merge(const Params& P, DeviceInfo* dev, cudaStream_t stream) {
 
 static int launch_by_dtype(Params& P, int dtype, DeviceInfo* dev, cudaStream_t stream) {
   switch (dtype) {
-    case GR_DTYPE_F32: return launch_fused<float>(P, dev, 0, stream);
-    case GR_DTYPE_BF16: return launch_fused<__nv_bfloat16>(P, dev, 1, stream);
-    case GR_DTYPE_F16: return launch_fused<__half>(P, dev, 2, stream);
+    case GR_DTYPE_F32: return launch_step_kernel<float>(P, dev, 0, stream);
+    case GR_DTYPE_BF16: return launch_step_kernel<__nv_bfloat16>(P, dev, 1, stream);
+    case GR_DTYPE_F16: return launch_step_kernel<__half>(P, dev, 2, stream);
     default: return GR_ERR_DTYPE;
   }
 }

@@ -27,6 +27,7 @@ constexpr int kPenTableMax = 1024;            // max history tokens with penalti
 constexpr int kSlack = 64;                    // extra keys kept by streamed top-k
 constexpr int kMaxBitmapWords = 8192;         // penalties: local vocab <= 262144
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s per wait
+constexpr uint32_t kWaitSleepNs = 100000u;                    // longest sleep per try (0.1 ms)
 
 constexpr float kLog2e = 1.4426950408889634f;
 #define kInf (__int_as_float(0x7f800000))
@@ -73,6 +74,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_try_wait, but the thread may sleep (not spin) for up to hint_ns
+// nanoseconds; it wakes as soon as the phase completes.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -86,7 +101,8 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    // sleep rather than spin, so that waiting warps leave the issue slots to the others
+    if (mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) return true;
     if (abort != nullptr && *abort) return false;
     if (global_timer_ns() - t0 > kWaitLimitNs) return false;
   }
@@ -107,6 +123,15 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// As bulk_copy_g2s with the default L2 policy (the bytes are read again soon).
+__device__ __forceinline__ void bulk_copy_g2s_keep(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 
