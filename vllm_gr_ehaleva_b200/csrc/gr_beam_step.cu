@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 #include <mutex>
 #include <type_traits>
+#include <utility>
 
 #include "../../include/gr_beam.h"
 #include "gr_device.cuh"
@@ -107,8 +108,15 @@ struct Params {
 // row_meta_kernel before the fused kernel so that a row's setup is one
 // prefetched load instead of a chain of dependent loads.
 constexpr int kMetaSmall = 16;                  // child tokens kept for small nodes
-constexpr int kMetaWords = 8 + kMetaSmall;      // 96 bytes
-enum MetaWord { kMNode = 0, kMCum = 1, kMC0 = 2, kMC1 = 3, kMLo = 4, kMHi = 5, kMTeff = 6, kMToks = 8 };
+constexpr int kMetaWords = 32;                  // 128 bytes
+enum MetaWord {
+  kMNode = 0, kMCum = 1, kMC0 = 2, kMC1 = 3, kMLo = 4, kMHi = 5,   // node, cum, CSR range, child token bounds
+  kMTeff = 6, kMRteff = 7,                                          // effective temperature and its reciprocal
+  kMRow = 8, kMR = 9, kMB = 10,                                     // row, request, beam
+  kMToks = 12,                                                      // child tokens of small nodes (16 words)
+  kMTauLo = 28, kMTauHi = 29                                        // request threshold (filled on chip)
+};
+static_assert(kMToks + kMetaSmall <= kMTauLo, "record layout");
 
 struct Scalars {
   int meta[kMetaWords];        // the current row's record
@@ -455,15 +463,19 @@ struct Step {
     }
   }
 
-  // Score one child candidate; returns its key (0 if not a local column).
-  __device__ __forceinline__ uint64_t child_key(const RowCtx& c, int tok, float x, float lse, uint32_t fb) const {
+  // Score child j (CSR position within the node, token tok) of a catalog row.
+  // Its key carries parent * V + j: children are sorted by token, so this
+  // orders ties exactly as parent * V + token does, and the merge reads the
+  // token and the child node at c0 + j without a search.
+  __device__ __forceinline__ uint64_t child_key(const RowCtx& c, int tok, int j, float x, float lse,
+                                                uint32_t fb) const {
     const float y = exact_y(c, x, tok - P.voff);
     float sc = __fadd_rn(c.cum, __fsub_rn(y, lse));
     if (tok == P.eos) {
       if (P.eos_score) P.eos_score[c.row] = sc;
       sc = -kInf;
     }
-    return make_key(sc, fb + static_cast<uint32_t>(tok));
+    return make_key(sc, fb + static_cast<uint32_t>(j));
   }
 
   __device__ void constrained_candidates(const RowCtx& cref, float lse) {
@@ -479,11 +491,75 @@ struct Step {
     const bool dense_window = c.dense && !processed_div && first >= c.wlo && first + deg - 1 <= c.whi;
     const int d0 = first - c.wlo;               // window index of the first child
     static_assert(kBatch == kThreads * 8, "dense path: one 8-entry group per thread per batch");
-    if (dense_window) {
+    bool dense_done = false;
+    constexpr int kG = 4;   // the one-pass dense scan covers kG * kBatch window entries
+    if (dense_window && d0 + deg <= kG * kBatch && S.v->thr_key != 0ull) {
+      // one pass over every child with a single reservation per warp; if the key
+      // list overflows (a weak bound), the batched loop below redoes the row
+      const uint64_t thr = S.v->thr_key;
+      const float thr_s = key_score(thr);
+      uint32_t pm[kG];
+      uint32_t cnt_t = 0;
+#pragma unroll
+      for (int g = 0; g < kG; ++g) {
+        pm[g] = 0;
+        const int w0 = g * kBatch + static_cast<int>(threadIdx.x) * 8;
+        const int i0 = w0 - d0;
+        if (w0 < d0 + deg) {
+          float x[8];
+          win_load8(w0, x);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float sc = __fadd_rn(c.cum, __fsub_rn(x[i], lse));
+            if (i0 + i >= 0 && i0 + i < deg && (sc >= thr_s || c.lo_tok + i0 + i == P.eos)) {
+              if (child_key(c, c.lo_tok + i0 + i, i0 + i, x[i], lse, fb) >= thr) pm[g] |= 1u << i;
+            }
+          }
+        }
+        cnt_t += static_cast<uint32_t>(__popc(pm[g]));
+      }
+      uint32_t pos = warp_reserve(cnt_t, &S.v->cnt);
+#pragma unroll
+      for (int g = 0; g < kG; ++g) {
+        if (pm[g]) {
+          const int w0 = g * kBatch + static_cast<int>(threadIdx.x) * 8;
+          const int i0 = w0 - d0;
+          float x[8];
+          win_load8(w0, x);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if ((pm[g] >> i) & 1u) {
+              if (pos < static_cast<uint32_t>(kKeyCap))
+                S.keys[pos] = child_key(c, c.lo_tok + i0 + i, i0 + i, x[i], lse, fb);
+              else
+                S.v->overflow = 1;
+              ++pos;
+            }
+          }
+        }
+      }
+      csync();
+      if (S.v->overflow == 0) {
+        dense_done = true;
+      } else {
+        csync();
+        if (threadIdx.x == 0) {
+          S.v->cnt = 0;
+          S.v->overflow = 0;
+        }
+        csync();
+      }
+    }
+    if (dense_done) {
+      // every child was scored in the one pass
+    } else if (dense_window) {
       // child j sits at window index d0 + j: 8 window entries per thread per 16-byte load
       for (int base = 0; base < d0 + deg; base += kBatch) {
         const uint64_t thr = S.v->thr_key;
         const float thr_s = thr ? key_score(thr) : -kInf;
+        // other rows of the request raise its bound meanwhile: read it for the next batch
+        uint64_t tau_g = 0;
+        if (threadIdx.x == 0 && base + kBatch < d0 + deg) tau_g = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
         const int w0 = base + static_cast<int>(threadIdx.x) * 8;   // kBatch == kThreads * 8
         const int i0 = w0 - d0;                                     // child index of entry w0
         float x[8];
@@ -502,17 +578,19 @@ struct Step {
           for (int i = 0; i < 8; ++i) p[i] = false;
         }
         if (__any_sync(0xFFFFFFFFu, any)) {
+          uint64_t kv[8];
+          uint32_t mask = 0;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            uint64_t key = 0;
-            bool pred = p[i];
-            if (pred) {
-              key = child_key(c, c.lo_tok + i0 + i, x[i], lse, fb);
-              pred = key >= thr;
+            kv[i] = 0;
+            if (p[i]) {
+              kv[i] = child_key(c, c.lo_tok + i0 + i, i0 + i, x[i], lse, fb);
+              if (kv[i] >= thr) mask |= 1u << i;
             }
-            warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
           }
+          warp_append_n<8>(mask, kv, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
         }
+        if (threadIdx.x == 0 && tau_g > S.v->thr_key) S.v->thr_key = tau_g;
         csync();
         if (base + kBatch < d0 + deg && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
           const Cut cut = shrink_to(P.k2);
@@ -525,6 +603,8 @@ struct Step {
         const int end = min(base + kBatch, c1);
         const uint64_t thr = S.v->thr_key;
         const float thr_s = thr ? key_score(thr) : -kInf;
+        uint64_t tau_g = 0;
+        if (threadIdx.x == 0 && end < c1) tau_g = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
         // issue every child-token load of the batch before using any of them
         int toks[kPer];
 #pragma unroll
@@ -559,17 +639,19 @@ struct Step {
           any |= p[i];
         }
         if (__any_sync(0xFFFFFFFFu, any)) {
+          uint64_t kv[kPer];
+          uint32_t mask = 0;
 #pragma unroll
           for (int i = 0; i < kPer; ++i) {
-            uint64_t key = 0;
-            bool pred = p[i];
-            if (pred) {
-              key = child_key(c, toks[i], xs[i], lse, fb);
-              pred = key >= thr;
+            kv[i] = 0;
+            if (p[i]) {
+              kv[i] = child_key(c, toks[i], base + i * kThreads + static_cast<int>(threadIdx.x) - c0, xs[i], lse, fb);
+              if (kv[i] >= thr) mask |= 1u << i;
             }
-            warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
           }
+          warp_append_n<kPer>(mask, kv, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
         }
+        if (threadIdx.x == 0 && tau_g > S.v->thr_key) S.v->thr_key = tau_g;
         csync();
         if (end < c1 && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
           const Cut cut = shrink_to(P.k2);
@@ -773,7 +855,7 @@ __device__ __forceinline__ void fill_row_ctx(const Params& P, const int* rec, Ro
   }
   c.cum = __int_as_float(rec[kMCum]);
   c.teff = __int_as_float(rec[kMTeff]);
-  c.rteff = __frcp_rn(c.teff);
+  c.rteff = __int_as_float(rec[kMRteff]);
   // penalties matter for processed log-probs and for the per-beam top-K's greedy token
   const bool pen_used = P.pen && P.T > 0 &&
                         (P.partial_only ? P.mode == kModeProcessed : (P.mode == kModeProcessed || P.K > 0));
@@ -889,8 +971,10 @@ done:
 // One thread per row: node -> CSR range -> child-token bounds (and, for small
 // nodes, every child token).
 __global__ void __launch_bounds__(256) row_meta_kernel(const __grid_constant__ Params P) {
+  pdl_trigger();   // the step kernel may start its prologue; it waits for this grid before reading
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= P.R * P.NB) return;
+  if (row % P.NB == 0) P.tau[row / P.NB] = 0ull;   // the request's running bound starts empty
   int w[kMetaWords];
 #pragma unroll
   for (int i = 0; i < kMetaWords; ++i) w[i] = 0;
@@ -899,9 +983,15 @@ __global__ void __launch_bounds__(256) row_meta_kernel(const __grid_constant__ P
     atomicOr(P.err, GR_DEVERR_BAD_NODE);
     node = GR_NODE_DEAD;
   }
+  const int r = row / P.NB;
+  const float teff = (P.mode == kModeProcessed) ? eff_temperature(P, r) : 1.0f;
   w[kMNode] = node;
   w[kMCum] = __float_as_int(P.cum[row]);
-  w[kMTeff] = __float_as_int((P.mode == kModeProcessed) ? eff_temperature(P, row / P.NB) : 1.0f);
+  w[kMTeff] = __float_as_int(teff);
+  w[kMRteff] = __float_as_int(__frcp_rn(teff));
+  w[kMRow] = row;
+  w[kMR] = r;
+  w[kMB] = row - r * P.NB;
   if (node >= 0) {
     const int c0 = static_cast<int>(P.row_ptr[node]);
     const int c1 = static_cast<int>(P.row_ptr[node + 1]);
@@ -947,6 +1037,8 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
   if (P.pen)
     for (int i = tid; i < P.bm_words; i += kBlock) S.bitmap[i] = 0u;
   GR_PROF_INIT();
+  pdl_wait();        // row metadata and the zeroed bounds come from the previous kernel
+  pdl_trigger();
   __syncthreads();   // the only CTA-wide barrier: consumers use csync() from here on
 
   if (warp == kWarps) {
@@ -1294,19 +1386,26 @@ drain:
 // sorts them and writes candidates, new beams with their child trie nodes and
 // the forked token table (serving_engine.py:566-590, llm.py:256-276).
 constexpr int kMergeMaxBeams = 4096;
-constexpr int kMergeCap = 16384;     // request candidates gathered into shared memory at once
+constexpr int kMergeCap = 16384;         // request candidates gathered into shared memory at once
+constexpr int kMergeTop = kKeyCap / 2;   // the kept keys (k2 <= kKeyCap / 2)
 
 struct MergeSmem {
-  uint64_t* keys;      // [kMergeCap]
-  uint32_t* prefix;    // [NB + 1] exclusive prefix of the row counts
+  uint64_t* keys;      // [kMergeCap] gathered keys
+  uint64_t* top;       // [kMergeTop] the kept top-2B
+  int* dec_tok;        // [kMergeTop] token of sorted candidate i
+  int* dec_par;        // [kMergeTop] parent beam of sorted candidate i
+  uint32_t* prefix;    // [NB + 1] exclusive prefix of the rows' counts
+  uint32_t* rc;        // [NB] the rows' counts
+  uint16_t* row_of;    // [kMergeCap] row of gathered index i
   SelectScratch* sel;
   uint32_t* wsum;      // [kWarps]
-  uint32_t* cnt;
+  uint32_t* cnt;       // [4] gathered, kept, real total
 };
 
 __host__ __device__ inline size_t merge_smem_bytes(int NB) {
-  return align128(size_t(kMergeCap) * 8) + align128(size_t(NB + 1) * 4) + align128(sizeof(SelectScratch)) +
-         align128(kWarps * 4) + 128;
+  return align128(size_t(kMergeCap) * 8) + align128(size_t(kMergeTop) * 8) + 2 * align128(size_t(kMergeTop) * 4) +
+         align128(size_t(NB + 1) * 4) + align128(size_t(NB) * 4) + align128(size_t(kMergeCap) * 2) +
+         align128(sizeof(SelectScratch)) + align128(kWarps * 4) + 128;
 }
 
 __device__ __forceinline__ int row_of_index(const uint32_t* prefix, int NB, uint32_t i) {
@@ -1318,25 +1417,58 @@ __device__ __forceinline__ int row_of_index(const uint32_t* prefix, int NB, uint
   return lo;
 }
 
+// Trie child of (parent node, token) by a binary search of the CSR children
+// (rows whose keys carry the token: per-beam top-K steps).
+__device__ __forceinline__ int child_by_search(const Params& P, const int* rec, int tok) {
+  const int pn = rec[kMNode];
+  if (pn == GR_NODE_UNCONSTRAINED) return GR_NODE_UNCONSTRAINED;
+  if (pn < 0) return GR_NODE_DEAD;
+  int lo = rec[kMC0], hi = rec[kMC1];
+  const int c1 = hi;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(P.child_tok + mid) < tok) lo = mid + 1; else hi = mid;
+  }
+  return (lo < c1 && __ldg(P.child_tok + lo) == tok) ? __ldg(P.child_node + lo) : GR_NODE_DEAD;
+}
+
 __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__ Params P) {
   unsigned char* smem_raw = g_smem;
   MergeSmem M;
   {
     size_t o = 0;
     M.keys = reinterpret_cast<uint64_t*>(smem_raw + o); o += align128(size_t(kMergeCap) * 8);
+    M.top = reinterpret_cast<uint64_t*>(smem_raw + o); o += align128(size_t(kMergeTop) * 8);
+    M.dec_tok = reinterpret_cast<int*>(smem_raw + o); o += align128(size_t(kMergeTop) * 4);
+    M.dec_par = reinterpret_cast<int*>(smem_raw + o); o += align128(size_t(kMergeTop) * 4);
     M.prefix = reinterpret_cast<uint32_t*>(smem_raw + o); o += align128(size_t(P.NB + 1) * 4);
+    M.rc = reinterpret_cast<uint32_t*>(smem_raw + o); o += align128(size_t(P.NB) * 4);
+    M.row_of = reinterpret_cast<uint16_t*>(smem_raw + o); o += align128(size_t(kMergeCap) * 2);
     M.sel = reinterpret_cast<SelectScratch*>(smem_raw + o); o += align128(sizeof(SelectScratch));
     M.wsum = reinterpret_cast<uint32_t*>(smem_raw + o); o += align128(kWarps * 4);
     M.cnt = reinterpret_cast<uint32_t*>(smem_raw + o);
   }
   const int r = blockIdx.x, tid = threadIdx.x, lane = lane_id(), warp = warp_id();
   const int NB = P.NB, k2 = P.k2;
-  // ---- exclusive prefix of the per-row counts
+  pdl_wait();   // the step kernel's row slots, counts and bounds
+#ifdef GR_PHASE_PROFILE
+  long long mt[8];
+  int mq = 0;
+#define GR_MPROF() do { if (tid == 0 && mq < 8) mt[mq++] = clock64(); } while (0)
+#else
+#define GR_MPROF() do { } while (0)
+#endif
+  GR_MPROF();
+  // ---- per-row counts and their exclusive prefix
   const unsigned* cnt = P.rowcnt + static_cast<size_t>(r) * NB;
   const int per = (NB + kThreads - 1) / kThreads;
   const int b0 = min(tid * per, NB), b1 = min(b0 + per, NB);
   uint32_t local = 0;
-  for (int b = b0; b < b1; ++b) local += min(__ldcg(cnt + b), static_cast<unsigned>(k2));
+  for (int b = b0; b < b1; ++b) {
+    const uint32_t c = min(__ldcg(cnt + b), static_cast<unsigned>(k2));
+    M.rc[b] = c;
+    local += c;
+  }
   uint32_t inc = local;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -1344,6 +1476,10 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     if (lane >= o) inc += v;
   }
   if (lane == 31) M.wsum[warp] = inc;
+  if (tid == 0) {
+    M.cnt[0] = 0;
+    M.cnt[1] = 0;
+  }
   csync();
   if (tid == 0) {
     uint32_t acc = 0;
@@ -1353,78 +1489,132 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
       acc += t;
     }
     M.prefix[NB] = acc;
-    *M.cnt = 0;
   }
   csync();
   uint32_t base = M.wsum[warp] + inc - local;
   for (int b = b0; b < b1; ++b) {
     M.prefix[b] = base;
-    base += min(__ldcg(cnt + b), static_cast<unsigned>(k2));
+    base += M.rc[b];
   }
   csync();
-  const int n = static_cast<int>(M.prefix[NB]);
-  const int k = min(k2, n);
+  const int n_all = static_cast<int>(M.prefix[NB]);
+  int k = min(k2, n_all);
+  // the request's final bound: at least 2B gathered keys are >= it (it is the
+  // 2B-th key of some row's own list), so smaller keys take no part
+  const uint64_t tau = __ldcg(P.tau + r);
   const unsigned long long* slots = P.buf + static_cast<size_t>(r) * NB * static_cast<size_t>(k2);
   const uint32_t* prefix = M.prefix;
-  auto keyf = [slots, prefix, NB, k2](int i) -> uint64_t {
-    const int b = row_of_index(prefix, NB, static_cast<uint32_t>(i));
-    return __ldcg(slots + static_cast<size_t>(b) * k2 + (static_cast<uint32_t>(i) - prefix[b]));
-  };
-  // ---- canonical top-2B
+  const uint32_t* rc = M.rc;
   int dummy = 0;
-  if (n <= kMergeCap) {
-    // gather every row slot into shared memory (one warp per row, coalesced)
-    for (int b = warp; b < NB; b += kWarps) {
-      const int c = static_cast<int>(M.prefix[b + 1] - M.prefix[b]);
-      const unsigned long long* src = slots + static_cast<size_t>(b) * k2;
-      uint64_t* dst = M.keys + M.prefix[b];
-      for (int j = lane; j < c; j += 32) dst[j] = __ldcg(src + j);
+  GR_MPROF();
+  // ---- canonical top-2B
+  int n = 0;   // keys >= tau gathered into shared memory
+  if (n_all <= kMergeCap) {
+    // row of every gathered index (one warp per row), then a flat gather with
+    // kU independent loads per thread in flight
+    for (int b = warp; b < NB; b += kWarps)
+      for (uint32_t j = lane; j < rc[b]; j += 32) M.row_of[prefix[b] + j] = static_cast<uint16_t>(b);
+    csync();
+    constexpr int kU = 16;
+    for (int base0 = 0; base0 < n_all; base0 += kThreads * kU) {
+      uint64_t kv[kU];
+      uint32_t mask = 0;
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int i = base0 + u * kThreads + tid;
+        kv[u] = 0ull;
+        if (i < n_all) {
+          const int b = M.row_of[i];
+          kv[u] = __ldcg(slots + static_cast<size_t>(b) * k2 + (static_cast<uint32_t>(i) - prefix[b]));
+          if (kv[u] >= tau) mask |= 1u << u;
+        }
+      }
+      warp_append_n<kU>(mask, kv, M.keys, &M.cnt[0], kMergeCap, &dummy);
     }
     csync();
-    if (n > k) {
-      uint64_t* keys = M.keys;
-      const Cut cut = cta_radix_select([keys](int i) { return keys[i]; }, n, k, M.sel);
-      // compact in rounds of one key per thread: writes never pass the keys read so far
-      for (int base = 0; base < n; base += kThreads) {
-        const int i = base + tid;
-        const uint64_t key = (i < n) ? keys[i] : 0ull;
-        const bool keep = (i < n) && cut.keep(key);
-        csync();
-        warp_append(keep, key, keys, M.cnt, kMergeCap, &dummy);
+    n = static_cast<int>(M.cnt[0]);
+    k = min(k, n);
+    GR_MPROF();
+    uint64_t* keys = M.keys;
+    Cut cut{0ull, 0};   // keeps every key
+    if (n > k) cut = cta_radix_select([keys](int i) { return keys[i]; }, n, k, M.sel);
+    GR_MPROF();
+    constexpr int kC = 16;
+    for (int base0 = 0; base0 < n; base0 += kThreads * kC) {
+      uint64_t kv[kC];
+      uint32_t mask = 0;
+#pragma unroll
+      for (int u = 0; u < kC; ++u) {
+        const int i = base0 + u * kThreads + tid;
+        kv[u] = (i < n) ? keys[i] : 0ull;
+        if (i < n && cut.keep(kv[u])) mask |= 1u << u;
       }
-      csync();
+      warp_append_n<kC>(mask, kv, M.top, &M.cnt[1], kMergeTop, &dummy);
     }
+    csync();
   } else {
+    auto keyf = [slots, prefix, NB, k2](int i) -> uint64_t {
+      const int b = row_of_index(prefix, NB, static_cast<uint32_t>(i));
+      return __ldcg(slots + static_cast<size_t>(b) * k2 + (static_cast<uint32_t>(i) - prefix[b]));
+    };
+    GR_MPROF();
     Cut cut{0ull, 0};
-    if (n > k) cut = cta_radix_select(keyf, n, k, M.sel);
-    for (int ib = warp * 32; ib < n; ib += kThreads) {
+    if (n_all > k) cut = cta_radix_select(keyf, n_all, k, M.sel);
+    GR_MPROF();
+    for (int ib = warp * 32; ib < n_all; ib += kThreads) {
       const int i = ib + lane;
-      uint64_t key = 0;
-      bool pred = false;
-      if (i < n) {
-        key = keyf(i);
-        pred = (n <= k) || cut.keep(key);
-      }
-      warp_append(pred, key, M.keys, M.cnt, kMergeCap, &dummy);
+      const uint64_t key = (i < n_all) ? keyf(i) : 0ull;
+      warp_append(i < n_all && cut.keep(key), key, M.top, &M.cnt[1], kMergeTop, &dummy);
     }
     csync();
   }
-  int P2 = 1;
-  while (P2 < k) P2 <<= 1;
-  for (int i = k + tid; i < P2; i += kThreads) M.keys[i] = 0ull;
-  csync();
-  cta_bitonic_sort_desc(M.keys, P2);
+  GR_MPROF();
+  // ---- descending order: rank sort for small k, bitonic otherwise
+  if (k <= kThreads) {
+    const uint64_t mine = (tid < k) ? M.top[tid] : 0ull;
+    int rank = 0;
+    int j = 0;
+    for (; j + 8 <= k; j += 8) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) rank += (M.top[j + u] > mine);
+    }
+    for (; j < k; ++j) rank += (M.top[j] > mine);
+    if (tid < k) M.keys[rank] = mine;
+    csync();
+  } else {
+    int P2 = 1;
+    while (P2 < k) P2 <<= 1;
+    for (int i = tid; i < P2; i += kThreads) M.keys[i] = (i < k) ? M.top[i] : 0ull;
+    csync();
+    cta_bitonic_sort_desc(M.keys, P2);
+  }
+  GR_MPROF();
   // ---- outputs
   const int B = P.B, T = P.T;
   for (int i = tid; i < k2; i += kThreads) {
     float sc = -kInf;
-    int tok = -1, par = -1;
+    int tok = -1, par = -1, child = GR_NODE_DEAD;
     if (i < k) {
       const uint64_t key = M.keys[i];
       const uint32_t flat = key_flat(key);
       sc = key_score(key);
-      tok = static_cast<int>(flat % static_cast<uint32_t>(P.V));
       par = static_cast<int>(flat / static_cast<uint32_t>(P.V));
+      const int x = static_cast<int>(flat - static_cast<uint32_t>(par) * static_cast<uint32_t>(P.V));
+      const int* rec = P.meta + static_cast<size_t>(r * NB + par) * kMetaWords;
+      const int pn = __ldcg(rec + kMNode);
+      if (P.K == 0 && pn >= 0) {
+        // catalog row: the key carries the child's CSR position
+        const int e = __ldcg(rec + kMC0) + x;
+        tok = __ldg(P.child_tok + e);
+        if (i < B) child = __ldg(P.child_node + e);
+      } else {
+        tok = x;
+        if (i < B) child = (pn == GR_NODE_UNCONSTRAINED) ? GR_NODE_UNCONSTRAINED : child_by_search(P, rec, tok);
+      }
+    }
+    if (i < kMergeTop) {
+      M.dec_tok[i] = tok;
+      M.dec_par[i] = par;
     }
     P.cand_score[static_cast<size_t>(r) * k2 + i] = sc;
     P.cand_token[static_cast<size_t>(r) * k2 + i] = tok;
@@ -1433,39 +1623,27 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
       P.sel_score[static_cast<size_t>(r) * B + i] = sc;
       P.sel_token[static_cast<size_t>(r) * B + i] = tok;
       P.sel_parent[static_cast<size_t>(r) * B + i] = par;
-      int child = GR_NODE_DEAD;
-      if (par >= 0) {
-        const int pn = P.node[r * NB + par];
-        if (pn == GR_NODE_UNCONSTRAINED) {
-          child = GR_NODE_UNCONSTRAINED;
-        } else if (pn >= 0 && pn < P.N) {
-          int lo = static_cast<int>(P.row_ptr[pn]);
-          const int hi0 = static_cast<int>(P.row_ptr[pn + 1]);
-          int hi = hi0;
-          while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            if (P.child_tok[mid] < tok) lo = mid + 1; else hi = mid;
-          }
-          if (lo < hi0 && P.child_tok[lo] == tok) child = P.child_node[lo];
-        }
-      }
       P.sel_node[static_cast<size_t>(r) * B + i] = child;
     }
   }
   if (P.hist_out) {
+    csync();
     const int W = T + 1;
     for (int idx = tid; idx < B * W; idx += kThreads) {
       const int i = idx / W, t = idx - i * W;
       int v = -1;
       if (i < k) {
-        const uint32_t flat = key_flat(M.keys[i]);
-        const int par = static_cast<int>(flat / static_cast<uint32_t>(P.V));
-        v = (t < T) ? P.hist[(static_cast<size_t>(r) * NB + par) * T + t]
-                    : static_cast<int>(flat % static_cast<uint32_t>(P.V));
+        const int par = M.dec_par[i];
+        v = (t < T) ? P.hist[(static_cast<size_t>(r) * NB + par) * T + t] : M.dec_tok[i];
       }
       P.hist_out[static_cast<size_t>(r) * B * W + idx] = v;
     }
   }
+#ifdef GR_PHASE_PROFILE
+  GR_MPROF();
+  if (tid == 0 && r < 512)   // merge counters sit after the step kernels' CTAs
+    for (int q = 1; q < mq; ++q) g_phase[512 + r][q] += static_cast<unsigned long long>(mt[q] - mt[q - 1]);
+#endif
 }
 
 // ============================================================== host side
@@ -1626,9 +1804,26 @@ static int launch_fused(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream_t 
   const int total = P.R * P.NB;
   const int slots = dev->sms * per;
   const int grid = total < slots ? total : slots;
-  fused_step_kernel<TL><<<grid, kBlock, smem, stream>>>(P);
-  if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
+  if (launch_pdl(fused_step_kernel<TL>, dim3(grid), dim3(kBlock), smem, stream, P) != cudaSuccess) return GR_ERR_CUDA;
   return GR_OK;
+}
+
+// Launch with programmatic stream serialization (the kernel calls pdl_wait()
+// before it reads what the previous kernel in the stream wrote).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // The warp-specialised kernel takes steps whose rows need no streamed
@@ -1666,8 +1861,8 @@ static int launch_fused_ws(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream
   }
   const int total = P.R * P.NB;
   const int grid = total < dev->sms ? total : dev->sms;
-  fused_step_ws_kernel<TL><<<grid, ws::kBlockWs, smem, stream>>>(P);
-  if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
+  if (launch_pdl(fused_step_ws_kernel<TL>, dim3(grid), dim3(ws::kBlockWs), smem, stream, P) != cudaSuccess)
+    return GR_ERR_CUDA;
   return GR_OK;
 }
 
@@ -1687,8 +1882,7 @@ static int launch_merge(const Params& P, DeviceInfo* dev, cudaStream_t stream) {
       return GR_ERR_CUDA;
     dev->merge_attr_set = true;
   }
-  merge_kernel<<<P.R, kThreads, smem, stream>>>(P);
-  if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
+  if (launch_pdl(merge_kernel, dim3(P.R), dim3(kThreads), smem, stream, P) != cudaSuccess) return GR_ERR_CUDA;
   return GR_OK;
 }
 
@@ -1766,7 +1960,6 @@ int32_t gr_beam_step(const gr_step_desc* d, const gr_step_io* io, void* workspac
   P.buf = reinterpret_cast<unsigned long long*>(ws + ws_tau_bytes(R) + ws_cnt_bytes(R, d->num_beams) +
                                                 ws_meta_bytes(R, d->num_beams));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(ws, 0, size_t(R) * 8, s) != cudaSuccess) return GR_ERR_CUDA;
   {
     const int rows = R * d->num_beams;
     row_meta_kernel<<<(rows + 255) / 256, 256, 0, s>>>(P);

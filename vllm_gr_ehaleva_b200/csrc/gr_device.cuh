@@ -101,8 +101,12 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
+#ifdef GR_WAIT_SLEEP
     // sleep rather than spin, so that waiting warps leave the issue slots to the others
     if (mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) return true;
+#else
+    if (mbar_try_wait(bar, parity)) return true;
+#endif
     if (abort != nullptr && *abort) return false;
     if (global_timer_ns() - t0 > kWaitLimitNs) return false;
   }
@@ -205,6 +209,63 @@ __device__ __forceinline__ void warp_append(bool pred, uint64_t key, uint64_t* k
   }
 }
 
+// Append the keys kv[i] with bit i of `mask` set (N per lane) with one
+// reservation for the whole warp: a warp scan of the lanes' counts gives each
+// lane its offset.  Must be called by all 32 lanes of the warp.
+template <int N>
+__device__ __forceinline__ void warp_append_n(uint32_t mask, const uint64_t (&kv)[N], uint64_t* keys, uint32_t* cnt,
+                                              uint32_t cap, int* overflow) {
+  const int lane = lane_id();
+  const uint32_t c = static_cast<uint32_t>(__popc(mask));
+  uint32_t inc = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += v;
+  }
+  const uint32_t total = __shfl_sync(0xFFFFFFFFu, inc, 31);
+  if (total == 0) return;
+  uint32_t base = 0;
+  if (lane == 31) base = atomicAdd(cnt, total);
+  base = __shfl_sync(0xFFFFFFFFu, base, 31);
+  uint32_t pos = base + inc - c;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    if ((mask >> i) & 1u) {
+      if (pos < cap)
+        keys[pos] = kv[i];
+      else
+        *overflow = 1;
+      ++pos;
+    }
+  }
+}
+
+// Reserve c slots per lane in a shared list with one atomic per warp; returns
+// this lane's first slot.  Must be called by all 32 lanes of the warp.
+__device__ __forceinline__ uint32_t warp_reserve(uint32_t c, uint32_t* cnt) {
+  const int lane = lane_id();
+  uint32_t inc = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += v;
+  }
+  const uint32_t total = __shfl_sync(0xFFFFFFFFu, inc, 31);
+  uint32_t base = 0;
+  if (lane == 31 && total > 0) base = atomicAdd(cnt, total);
+  base = __shfl_sync(0xFFFFFFFFu, base, 31);
+  return base + inc - c;
+}
+
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start before its predecessor in the stream has finished;
+// pdl_wait() blocks until the predecessor grid has completed and its memory is
+// visible (a no-op for an ordinary launch), pdl_trigger() lets the successor
+// grid launch early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- radix select
 // Keys kept by a selection: (key >> shift) >= (prefix >> shift).
 struct Cut {
@@ -235,16 +296,10 @@ __device__ Cut cta_radix_select(KeyFn keyf, int n, int k, SelectScratch* sc) {
     for (int i = threadIdx.x; i < 256; i += kThreads) sc->hist[i] = 0;
     csync();
     const int hs = shift + 8;
-    for (int ib = warp_id() * 32; ib < n; ib += kThreads) {
-      const int i = ib + lane;
-      uint32_t digit = 256u;
-      if (i < n) {
-        const uint64_t key = keyf(i);
-        const bool match = (hs >= 64) || ((key >> hs) == (prefix >> hs));
-        if (match) digit = static_cast<uint32_t>((key >> shift) & 0xFFu);
-      }
-      const unsigned peers = __match_any_sync(0xFFFFFFFFu, digit);
-      if (digit < 256u && lane == __ffs(peers) - 1) atomicAdd(&sc->hist[digit], static_cast<uint32_t>(__popc(peers)));
+    // plain shared-memory atomics (measured faster here than match-based aggregation)
+    for (int i = threadIdx.x; i < n; i += kThreads) {
+      const uint64_t key = keyf(i);
+      if ((hs >= 64) || ((key >> hs) == (prefix >> hs))) atomicAdd(&sc->hist[(key >> shift) & 0xFFu], 1u);
     }
     csync();
     if (warp_id() == 0) {
@@ -300,12 +355,13 @@ __device__ __forceinline__ uint32_t cta_compact(uint64_t* keys, int n, Cut cut, 
   if (threadIdx.x == 0) *cnt = 0;
   csync();
   int dummy = 0;
+  uint32_t mask = 0;
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int i = threadIdx.x + j * kThreads;
-    const bool keep = (i < n) && cut.keep(reg[j]);
-    warp_append(keep, reg[j], keys, cnt, kKeyCap, &dummy);
+    if ((i < n) && cut.keep(reg[j])) mask |= 1u << j;
   }
+  warp_append_n<kPer>(mask, reg, keys, cnt, kKeyCap, &dummy);
   csync();
   return *cnt;
 }

@@ -24,7 +24,7 @@
 #pragma once
 
 #ifndef GR_WS_STREAM_WARPS
-#define GR_WS_STREAM_WARPS 12
+#define GR_WS_STREAM_WARPS 16
 #endif
 
 namespace ws {
@@ -107,12 +107,19 @@ __device__ void ws_produce(const Params& P, int my_n) {
   int stage = 0;
   uint32_t round = 0;
   long long fills = 0;
+  static_assert(kMetaWords == 32, "one record word per producer lane");
+  // the next row's record word (lane = word) and its request threshold (lane 0),
+  // loaded one row ahead
   int meta_word = 0;
-  if (my_n > 0 && lane < kMetaWords)
-    meta_word = __ldcg(P.meta + static_cast<size_t>(row_of_iter(P, 0)) * kMetaWords + lane);
+  unsigned long long tau_word = 0;
+  int row_next = (my_n > 0) ? row_of_iter(P, 0) : 0;
+  if (my_n > 0) {
+    meta_word = __ldcg(P.meta + static_cast<size_t>(row_next) * kMetaWords + lane);
+    if (lane == 0) tau_word = *reinterpret_cast<volatile unsigned long long*>(P.tau + row_next / P.NB);
+  }
   for (int it = 0; it < my_n; ++it) {
     const int slot = it & 1;
-    const int row = row_of_iter(P, it);
+    const int row = row_next;
     // the slot is free once the finishers are done with row it-2
     if (it >= 2) {
       WS_PROF_T(t_fd);
@@ -129,9 +136,14 @@ __device__ void ws_produce(const Params& P, int my_n) {
       }
     }
     const int cur = meta_word;
-    if (lane < kMetaWords) W.rec(slot)[lane] = cur;
-    if (it + 1 < my_n && lane < kMetaWords)
-      meta_word = __ldcg(P.meta + static_cast<size_t>(row_of_iter(P, it + 1)) * kMetaWords + lane);
+    const unsigned long long tau_cur = __shfl_sync(0xFFFFFFFFu, tau_word, 0);
+    W.rec(slot)[lane] = (lane == kMTauLo) ? static_cast<int>(tau_cur & 0xFFFFFFFFull)
+                      : (lane == kMTauHi) ? static_cast<int>(tau_cur >> 32) : cur;
+    if (it + 1 < my_n) {
+      row_next = row_of_iter(P, it + 1);
+      meta_word = __ldcg(P.meta + static_cast<size_t>(row_next) * kMetaWords + lane);
+      if (lane == 0) tau_word = *reinterpret_cast<volatile unsigned long long*>(P.tau + row_next / P.NB);
+    }
     const int node = __shfl_sync(0xFFFFFFFFu, cur, kMNode);
     const int c0 = __shfl_sync(0xFFFFFFFFu, cur, kMC0);
     const int c1 = __shfl_sync(0xFFFFFFFFu, cur, kMC1);
@@ -233,9 +245,8 @@ __device__ void ws_stream_rows(const Params& P, int my_n) {
       aborted = true;
       break;
     }
-    const int row = row_of_iter(P, it);
-    const float teff = __int_as_float(W.rec(slot)[kMTeff]);
-    const float yscale = (P.mode == kModeProcessed) ? __frcp_rn(teff) : 1.0f;
+    const int row = W.rec(slot)[kMRow];
+    const float yscale = (P.mode == kModeProcessed) ? __int_as_float(W.rec(slot)[kMRteff]) : 1.0f;
     const float a = kLog2e * yscale;
     float m = -kInf, s = 0.0f;
     const Geom g = row_geom<ES, ws::kStage>(P, row);
@@ -365,10 +376,6 @@ __device__ void ws_finish_rows(const Params& P, int my_n) {
   constexpr int EPV = Tr::kPerVec;
   constexpr int kSubVecs = kBatch / EPV;
   const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
-  // the request's running threshold, read one row ahead (a stale bound is still valid)
-  uint64_t tau_next = 0;
-  if (tid == 0 && my_n > 0)
-    tau_next = *reinterpret_cast<volatile unsigned long long*>(P.tau + row_of_iter(P, 0) / P.NB);
   for (int it = 0; it < my_n; ++it) {
     const int slot = it & 1;
     const uint32_t par = static_cast<uint32_t>(it >> 1) & 1u;
@@ -382,10 +389,13 @@ __device__ void ws_finish_rows(const Params& P, int my_n) {
     WS_PROF_ADD(tid == 0, 2, t_rd);
     WS_PROF_T(t_fin);
     RowCtx c;
-    c.row = row_of_iter(P, it);
-    c.r = c.row / P.NB;
-    c.b = c.row - c.r * P.NB;
     const int* rec = W.rec(slot);
+    c.row = rec[kMRow];
+    c.r = rec[kMR];
+    c.b = rec[kMB];
+    // a fresh read of the request's running threshold, used at the end of the prelude
+    uint64_t tau_fresh = 0;
+    if (tid == 0) tau_fresh = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
     fill_row_ctx<TL>(P, rec, c);
     if (c.constrained) {
       c.wlo = W.win_lo[slot];
@@ -393,23 +403,27 @@ __device__ void ws_finish_rows(const Params& P, int my_n) {
     }
     st.rec = rec;
     st.win_off = slot ? ws::kWin1Off : 0;
-    // normaliser: every thread combines the partials in the same order
-    float M = -kInf;
+    WS_PROF_ADD(tid == 0, 13, t_fin);
+    // normaliser: lane w of every finisher warp takes streamer partial w; the
+    // same shuffle tree in every warp gives every thread the same value
+    static_assert(ws::kStrWarps <= 32, "one partial per lane");
+    const float pm = (lane < ws::kStrWarps) ? W.part_m(slot)[lane] : -kInf;
+    const float ps = (lane < ws::kStrWarps) ? W.part_s(slot)[lane] : 0.0f;
+    float M = pm;
 #pragma unroll
-    for (int w = 0; w < ws::kStrWarps; ++w) M = fmaxf(M, W.part_m(slot)[w]);
-    float tot = 0.0f;
-    if (M > -kInf) {
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+    float tot = (M > -kInf && lane < ws::kStrWarps) ? ps * fast_exp2((pm - M) * kLog2e) : 0.0f;
 #pragma unroll
-      for (int w = 0; w < ws::kStrWarps; ++w)
-        tot += W.part_s(slot)[w] * fast_exp2((W.part_m(slot)[w] - M) * kLog2e);
-    }
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, o);
     float lse = M + logf(tot);
     // an overflowing or NaN streamed sum (uniform: every finisher has the same tot)
     if (M > -kInf && !(tot <= 3.0e38f)) lse = ws_exact_row_lse<TL>(P, c, st);
+    WS_PROF_ADD(tid == 0, 14, t_fin);
     if (tid == 0) {
-      const uint64_t tau_pref = tau_next;
-      if (it + 1 < my_n)
-        tau_next = *reinterpret_cast<volatile unsigned long long*>(P.tau + row_of_iter(P, it + 1) / P.NB);
+      // the request's running threshold as the producer read it (a stale bound is still valid)
+      uint64_t tau_pref = static_cast<uint64_t>(static_cast<uint32_t>(rec[kMTauLo])) |
+                          (static_cast<uint64_t>(static_cast<uint32_t>(rec[kMTauHi])) << 32);
+      if (tau_fresh > tau_pref) tau_pref = tau_fresh;
       S.v->cnt = 0;
       S.v->overflow = 0;
       S.v->discard = 0;
@@ -420,10 +434,14 @@ __device__ void ws_finish_rows(const Params& P, int my_n) {
       if (P.lse_out) P.lse_out[c.row] = lse;
       if (P.eos_score) P.eos_score[c.row] = __int_as_float(0x7FC00000);
     }
+    WS_PROF_ADD(tid == 0, 15, t_fin);
     csync();
+    WS_PROF_ADD(tid == 0, 7, t_fin);
     if (W.fin_abort[slot]) break;
     if (c.constrained) {
+      WS_PROF_T(t_cc);
       st.constrained_candidates(c, lse);
+      WS_PROF_ADD(tid == 0, 12, t_cc);
     } else if (c.stream) {
       // a row without a catalog node: its selection needs the whole row, which
       // the streamers did not keep, so read it again (L2 or HBM)
@@ -511,6 +529,8 @@ __global__ void __launch_bounds__(ws::kBlockWs, 1) fused_step_ws_kernel(const __
     S.v->issued = 0;
   }
   GR_PROF_INIT();
+  pdl_wait();        // row metadata and the zeroed bounds come from the previous kernel
+  pdl_trigger();
   __syncthreads();
   if (warp == ws::kProdWarp) {
     ws_produce<TL>(P, my_n);
