@@ -179,23 +179,27 @@ int32_t gr_beam_step_noalloc(const gr_step_desc* desc, const gr_step_io* io, voi
 
 /* ---- vocab-sharded lm_head (logit columns split over ranks) --------------
  *
- * Phase 1 (every shard): per-row partial (max, sum exp(x - max)) over the
- * local columns, written as float2 pairs to partials[row] = {max, sumexp}.
- * Replaces the full-row log_softmax of vllm sampler.py:300-301 after the
- * tensor-parallel logits all-gather (vllm logits_processor.py:75-86).
+ * With the lm_head split by vocabulary columns, shard k holds columns
+ * [vocab_offset, vocab_offset + vocab_local) of every row (vLLM would
+ * all-gather the full logits first: vllm logits_processor.py:75-86).  A step
+ * becomes three calls with two all-gathers between them, all on the caller's
+ * stream; every call takes the gr_beam_step workspace (same size).
+ *
+ * Phase 1 (every shard): per-row partial (max, sum exp(y - max)) over the
+ * local columns, y the log-prob domain value (processed mode: penalties and
+ * temperature applied), written to partials[row][2] = {max, sumexp}.
+ * Replaces the full-row log_softmax of vllm sampler.py:300-301.
  */
-int32_t gr_lse_partials(const gr_step_desc* desc, const void* logits,
-                        const float* temperature, const float* rep_penalty,
-                        const float* pres_penalty, const float* freq_penalty,
-                        const int32_t* hist_in, float* partials,
-                        int32_t* err, void* stream);
+int32_t gr_lse_partials(const gr_step_desc* desc, const gr_step_io* io, float* partials,
+                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* Phase 2 (every shard, after the caller all-gathered the partials of all
  * `num_shards` shards into gathered_partials[num_shards][R*num_beams][2]):
- * combines them into the global row lse, forms this shard's candidates and
- * writes the shard's canonical top-2B per request to
- * shard_keys[R][2B] (uint64 keys, see gr_key_decode in the Python layer).
- * Constrained (per_beam_k == 0) mode only. */
+ * combines them into the rows' global lse (written to io->lse when it is not
+ * NULL), scores this shard's catalog children and writes the shard's
+ * canonical top-2B keys per request to shard_keys[R][2B] (zero = empty).
+ * io->eos_score is valid on the shard whose columns hold eos_token_id.
+ * Constrained (per_beam_k == 0) steps only. */
 int32_t gr_shard_candidates(const gr_step_desc* desc, const gr_step_io* io,
                             const float* gathered_partials, int32_t num_shards,
                             uint64_t* shard_keys, void* workspace,
@@ -203,11 +207,11 @@ int32_t gr_shard_candidates(const gr_step_desc* desc, const gr_step_io* io,
 
 /* Phase 3 (every shard, after the caller all-gathered shard_keys of all
  * shards into gathered_keys[num_shards][R][2B]): merges them into the global
- * top-2B per request and writes cand_* / sel_* / hist_out of `io` (the logits
- * field is unused).  Every shard computes the same result. */
+ * top-2B per request and writes cand_* / sel_* / sel_node / hist_out of `io`
+ * (the logits field is unused).  Every shard computes the same result. */
 int32_t gr_merge_candidates(const gr_step_desc* desc, const gr_step_io* io,
                             const uint64_t* gathered_keys, int32_t num_shards,
-                            void* stream);
+                            void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,111 @@
+"""Vocab-sharded step on one GPU: S column shards of the same logits run the
+three phases (lse partials, shard candidates, merge) with the all-gathers done
+by stacking.  The result must be the full-vocabulary step's: bit-exact against
+the oracle given the combined lse, and within the reference-arithmetic
+tolerance; every shard's merge must agree."""
+import numpy as np
+import pytest
+
+from helpers import OUT_KEYS, Case, assert_step_parity, make_logits, next_inputs, small_catalog, tiny_catalog_csr, \
+    to_device_logits
+from vllm_gr_ehaleva_b200.synthetic import initial_cum
+
+pytestmark = pytest.mark.gpu
+
+
+def sharded_gpu_step(case: Case, shards: int, device="cuda") -> dict:
+    import torch
+    from vllm_gr_ehaleva_b200 import sharded as SH
+    R, NB, V = case.R, case.NB, case.vocab_size
+    assert V % shards == 0
+    VL = V // shards
+    full = to_device_logits(case, device)                      # [R*NB, V]
+    local = [full[:, k * VL:(k + 1) * VL] for k in range(shards)]
+    cum = torch.from_numpy(case.cum).to(device)
+    node = torch.from_numpy(case.node).to(device)
+    csr = None
+    if case.csr is not None:
+        csr = tuple(torch.from_numpy(a).to(device) for a in (case.csr.row_ptr, case.csr.child_tok, case.csr.child_node))
+    hist = None if case.hist is None else torch.from_numpy(case.hist).to(device)
+    kw = dict(beam_width=case.beam_width, csr=csr, vocab_size=V, logprobs_mode=case.mode,
+              eos_token_id=None if case.eos < 0 else case.eos, hist=hist, temperature=case.temperature)
+    parts = [SH.lse_partials(local[k], cum, node, vocab_offset=k * VL, **kw) for k in range(shards)]
+    gathered_p = torch.stack(parts)
+    res = [SH.shard_candidates(local[k], cum, node, gathered_p, vocab_offset=k * VL, **kw) for k in range(shards)]
+    gathered_k = torch.stack([r[0] for r in res])
+    outs = [SH.merge_candidates(local[k], cum, node, gathered_k, vocab_offset=k * VL, **kw) for k in range(shards)]
+    torch.cuda.synchronize()
+    eos = res[0][2]
+    for k in range(1, shards):
+        eos = torch.where(torch.isnan(eos), res[k][2], eos)
+    got = {key: getattr(outs[0], key).cpu().numpy() for key in OUT_KEYS if key not in ("lse", "eos_score")}
+    got["lse"] = res[0][1].cpu().numpy()
+    got["eos_score"] = eos.cpu().numpy()
+    err = 0
+    for p in parts:
+        err |= int(p.err.item())
+    for r in res:
+        err |= int(r[3].item())
+    for o in outs:
+        err |= int(o.err.item())
+    got["err"] = err
+    # every shard computed the same normaliser and the same merged step
+    for k in range(1, shards):
+        assert np.array_equal(res[k][1].cpu().numpy().view(np.uint32), got["lse"].view(np.uint32))
+        for key in ("cand_score", "cand_token", "cand_parent", "sel_token", "sel_parent", "sel_node", "hist_out"):
+            assert np.array_equal(getattr(outs[k], key).cpu().numpy(), got[key]), key
+    return got
+
+
+@pytest.mark.parametrize("shards", [2, 4])
+def test_sharded_constrained_three_steps(shards):
+    cat = small_catalog()
+    R, NB, B, V = 3, 16, 16, 8192
+    node = np.full((R, NB), cat.start_node, np.int32)
+    node[1, 3] = -1                      # a row without a catalog node
+    node[2, 5] = -2                      # a dead row
+    case = Case(logits32=make_logits(R, NB, V, 4.0, 3, "bf16"), dtype="bf16", cum=initial_cum(R, NB), node=node,
+                beam_width=B, vocab_size=V, csr=cat.csr, hist=np.full((R, NB, 1), cat.sid_begin, np.int32))
+    for step in range(3):
+        got = sharded_gpu_step(case, shards)
+        assert_step_parity(case, got)
+        case = next_inputs(case, got, make_logits(R, NB, V, 4.0, 30 + step, "bf16"))
+
+
+def test_sharded_eos_child():
+    V, eos = 64, 5
+    csr = tiny_catalog_csr([[1, 2, 3], [1, 2, 40], [1, eos], [7, 8], [1, 33]])
+    start = csr.walk([1])
+    R, NB, B = 2, 3, 4
+    x = make_logits(R, NB, V, 2.0, 41, "f32")
+    node = np.array([[start, csr.walk([1, 2]), -2], [start, start, csr.walk([7])]], np.int32)
+    case = Case(logits32=x, dtype="f32", cum=np.array([[-1, -2, -3], [-0.5, -0.7, -4]], np.float32),
+                node=node, beam_width=B, vocab_size=V, csr=csr, eos=eos,
+                hist=np.arange(R * NB * 2, dtype=np.int32).reshape(R, NB, 2))
+    got = sharded_gpu_step(case, 2)
+    assert_step_parity(case, got)
+    assert np.isfinite(got["eos_score"][0, 0])
+
+
+def test_sharded_processed_temperature():
+    cat = small_catalog()
+    R, NB, B, V = 2, 8, 8, 8192
+    case = Case(logits32=make_logits(R, NB, V, 4.0, 9, "f32"), dtype="f32", cum=initial_cum(R, NB),
+                node=np.full((R, NB), cat.start_node, np.int32), beam_width=B, vocab_size=V, csr=cat.csr,
+                mode="processed_logprobs", temperature=[0.7, 1.3])
+    assert_step_parity(case, sharded_gpu_step(case, 2))
+
+
+@pytest.mark.slow
+def test_sharded_cfg5_geometry():
+    # cfg5's shard geometry (V = 152064 in 8 shards of 19008 columns, B = 128) on 2 requests
+    from vllm_gr_ehaleva_b200.synthetic import make_catalog
+    cat = make_catalog(200_000, 3, 8192, 152064, 1.1, seed=1)
+    R, NB, B, V = 2, 128, 128, 152064
+    case = Case(logits32=make_logits(R, NB, V, 4.0, 5, "bf16"), dtype="bf16", cum=initial_cum(R, NB),
+                node=np.full((R, NB), cat.start_node, np.int32), beam_width=B, vocab_size=V, csr=cat.csr,
+                hist=np.full((R, NB, 1), cat.sid_begin, np.int32))
+    for step in range(2):
+        got = sharded_gpu_step(case, 8)
+        assert_step_parity(case, got)
+        case = next_inputs(case, got, make_logits(R, NB, V, 4.0, 60 + step, "bf16"))

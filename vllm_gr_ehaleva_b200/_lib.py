@@ -90,15 +90,14 @@ def load(path: str | None = None) -> ctypes.CDLL:
     lib.gr_beam_step_noalloc.restype = ctypes.c_int32
     lib.gr_beam_step_noalloc.argtypes = [P(StepDesc), P(StepIO), ctypes.c_void_p]
     lib.gr_lse_partials.restype = ctypes.c_int32
-    lib.gr_lse_partials.argtypes = [P(StepDesc), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                                    ctypes.c_void_p, ctypes.c_void_p]
+    lib.gr_lse_partials.argtypes = [P(StepDesc), P(StepIO), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                    ctypes.c_void_p]
     lib.gr_shard_candidates.restype = ctypes.c_int32
     lib.gr_shard_candidates.argtypes = [P(StepDesc), P(StepIO), ctypes.c_void_p, ctypes.c_int32,
                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.gr_merge_candidates.restype = ctypes.c_int32
     lib.gr_merge_candidates.argtypes = [P(StepDesc), P(StepIO), ctypes.c_void_p, ctypes.c_int32,
-                                        ctypes.c_void_p]
+                                        ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     _lib = lib
     return lib
 

@@ -99,6 +99,11 @@ struct Params {
   int bm_words;
   int partial_only;   // 1: write (max, sumexp) partials only (vocab-sharded phase 1)
   float2* partials;
+  const float* lse_in;            // vocab-sharded phase 2: the rows' global normaliser (no streaming)
+  unsigned long long* keys_out;   // merge writes the sorted top-2B keys [R][2B] (zero padded) instead
+  // merge input grid: request r's slot s sits at buf + (r * slot_sr + s * slot_sb) * 2B
+  int slot_rows;
+  long long slot_sr, slot_sb;
 };
 
 // Shared-memory layout (dynamic shared memory).  Every piece but the ring sits
@@ -1319,6 +1324,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
         for (int w = 0; w < kWarps; ++w) tot += S.red_s[w] * fast_exp2((S.red_m[w] - M) * kLog2e);
       }
       lse = M + logf(tot);
+      if (P.lse_in) lse = P.lse_in[c.row];   // vocab-sharded phase 2: the global normaliser
       if (tid == 0) {
         if (P.lse_out) P.lse_out[c.row] = lse;
         if (P.partial_only) P.partials[c.row] = make_float2(M, tot);
@@ -1441,8 +1447,9 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     M.top = reinterpret_cast<uint64_t*>(smem_raw + o); o += align128(size_t(kMergeTop) * 8);
     M.dec_tok = reinterpret_cast<int*>(smem_raw + o); o += align128(size_t(kMergeTop) * 4);
     M.dec_par = reinterpret_cast<int*>(smem_raw + o); o += align128(size_t(kMergeTop) * 4);
-    M.prefix = reinterpret_cast<uint32_t*>(smem_raw + o); o += align128(size_t(P.NB + 1) * 4);
-    M.rc = reinterpret_cast<uint32_t*>(smem_raw + o); o += align128(size_t(P.NB) * 4);
+    const int rows = max(P.NB, P.slot_rows);
+    M.prefix = reinterpret_cast<uint32_t*>(smem_raw + o); o += align128(size_t(rows + 1) * 4);
+    M.rc = reinterpret_cast<uint32_t*>(smem_raw + o); o += align128(size_t(rows) * 4);
     M.row_of = reinterpret_cast<uint16_t*>(smem_raw + o); o += align128(size_t(kMergeCap) * 2);
     M.sel = reinterpret_cast<SelectScratch*>(smem_raw + o); o += align128(sizeof(SelectScratch));
     M.wsum = reinterpret_cast<uint32_t*>(smem_raw + o); o += align128(kWarps * 4);
@@ -1450,6 +1457,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
   }
   const int r = blockIdx.x, tid = threadIdx.x, lane = lane_id(), warp = warp_id();
   const int NB = P.NB, k2 = P.k2;
+  const int S = P.slot_rows;   // slots gathered per request (rows, or shards)
   pdl_wait();   // the step kernel's row slots, counts and bounds
 #ifdef GR_PHASE_PROFILE
   long long mt[8];
@@ -1459,13 +1467,13 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
 #define GR_MPROF() do { } while (0)
 #endif
   GR_MPROF();
-  // ---- per-row counts and their exclusive prefix
-  const unsigned* cnt = P.rowcnt + static_cast<size_t>(r) * NB;
-  const int per = (NB + kThreads - 1) / kThreads;
-  const int b0 = min(tid * per, NB), b1 = min(b0 + per, NB);
+  // ---- per-slot counts (no count array: every slot full, zero keys empty) and their exclusive prefix
+  const int per = (S + kThreads - 1) / kThreads;
+  const int b0 = min(tid * per, S), b1 = min(b0 + per, S);
   uint32_t local = 0;
   for (int b = b0; b < b1; ++b) {
-    const uint32_t c = min(__ldcg(cnt + b), static_cast<unsigned>(k2));
+    const uint32_t c = P.rowcnt ? min(__ldcg(P.rowcnt + static_cast<size_t>(r) * NB + b), static_cast<unsigned>(k2))
+                                : static_cast<uint32_t>(k2);
     M.rc[b] = c;
     local += c;
   }
@@ -1488,7 +1496,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
       M.wsum[w] = acc;
       acc += t;
     }
-    M.prefix[NB] = acc;
+    M.prefix[S] = acc;
   }
   csync();
   uint32_t base = M.wsum[warp] + inc - local;
@@ -1497,12 +1505,14 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     base += M.rc[b];
   }
   csync();
-  const int n_all = static_cast<int>(M.prefix[NB]);
+  const int n_all = static_cast<int>(M.prefix[S]);
   int k = min(k2, n_all);
   // the request's final bound: at least 2B gathered keys are >= it (it is the
   // 2B-th key of some row's own list), so smaller keys take no part
   const uint64_t tau = __ldcg(P.tau + r);
-  const unsigned long long* slots = P.buf + static_cast<size_t>(r) * NB * static_cast<size_t>(k2);
+  // slot b of this request starts at slots + b * slot_step
+  const unsigned long long* slots = P.buf + static_cast<size_t>(r) * P.slot_sr * static_cast<size_t>(k2);
+  const size_t slot_step = static_cast<size_t>(P.slot_sb) * static_cast<size_t>(k2);
   const uint32_t* prefix = M.prefix;
   const uint32_t* rc = M.rc;
   int dummy = 0;
@@ -1512,23 +1522,26 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
   if (n_all <= kMergeCap) {
     // row of every gathered index (one warp per row), then a flat gather with
     // kU independent loads per thread in flight
-    for (int b = warp; b < NB; b += kWarps)
+    for (int b = warp; b < S; b += kWarps)
       for (uint32_t j = lane; j < rc[b]; j += 32) M.row_of[prefix[b] + j] = static_cast<uint16_t>(b);
     csync();
     constexpr int kU = 16;
     for (int base0 = 0; base0 < n_all; base0 += kThreads * kU) {
-      uint64_t kv[kU];
-      uint32_t mask = 0;
+      // addresses first, then every load, then the uses: no load waits for another
+      const unsigned long long* src[kU];
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
-        const int i = base0 + u * kThreads + tid;
-        kv[u] = 0ull;
-        if (i < n_all) {
-          const int b = M.row_of[i];
-          kv[u] = __ldcg(slots + static_cast<size_t>(b) * k2 + (static_cast<uint32_t>(i) - prefix[b]));
-          if (kv[u] >= tau) mask |= 1u << u;
-        }
+        const int i = min(base0 + u * kThreads + tid, n_all - 1);
+        const int b = M.row_of[i];
+        src[u] = slots + static_cast<size_t>(b) * slot_step + (static_cast<uint32_t>(i) - prefix[b]);
       }
+      uint64_t kv[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) kv[u] = __ldcg(src[u]);
+      uint32_t mask = 0;
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (base0 + u * kThreads + tid < n_all && kv[u] >= tau && kv[u] != 0ull) mask |= 1u << u;
       warp_append_n<kU>(mask, kv, M.keys, &M.cnt[0], kMergeCap, &dummy);
     }
     csync();
@@ -1553,9 +1566,9 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     }
     csync();
   } else {
-    auto keyf = [slots, prefix, NB, k2](int i) -> uint64_t {
-      const int b = row_of_index(prefix, NB, static_cast<uint32_t>(i));
-      return __ldcg(slots + static_cast<size_t>(b) * k2 + (static_cast<uint32_t>(i) - prefix[b]));
+    auto keyf = [slots, prefix, S, slot_step](int i) -> uint64_t {
+      const int b = row_of_index(prefix, S, static_cast<uint32_t>(i));
+      return __ldcg(slots + static_cast<size_t>(b) * slot_step + (static_cast<uint32_t>(i) - prefix[b]));
     };
     GR_MPROF();
     Cut cut{0ull, 0};
@@ -1564,9 +1577,10 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     for (int ib = warp * 32; ib < n_all; ib += kThreads) {
       const int i = ib + lane;
       const uint64_t key = (i < n_all) ? keyf(i) : 0ull;
-      warp_append(i < n_all && cut.keep(key), key, M.top, &M.cnt[1], kMergeTop, &dummy);
+      warp_append(i < n_all && key != 0ull && cut.keep(key), key, M.top, &M.cnt[1], kMergeTop, &dummy);
     }
     csync();
+    k = min(k, static_cast<int>(M.cnt[1]));
   }
   GR_MPROF();
   // ---- descending order: rank sort for small k, bitonic otherwise
@@ -1589,6 +1603,11 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     cta_bitonic_sort_desc(M.keys, P2);
   }
   GR_MPROF();
+  if (P.keys_out) {
+    // vocab-sharded phase 2: this shard's canonical top-2B keys, zero padded
+    for (int i = tid; i < k2; i += kThreads) P.keys_out[static_cast<size_t>(r) * k2 + i] = (i < k) ? M.keys[i] : 0ull;
+    return;
+  }
   // ---- outputs
   const int B = P.B, T = P.T;
   for (int i = tid; i < k2; i += kThreads) {
@@ -1758,6 +1777,11 @@ static void fill_params(Params& P, const gr_step_desc* d, const gr_step_io* io) 
   P.bm_words = (d->vocab_local + 31) / 32 + 1;
   P.partial_only = 0;
   P.partials = nullptr;
+  P.lse_in = nullptr;
+  P.keys_out = nullptr;
+  P.slot_rows = d->num_beams;
+  P.slot_sr = d->num_beams;
+  P.slot_sb = 1;
 }
 
 // Two CTAs per SM when at least three ring stages fit beside the fixed
@@ -1830,7 +1854,7 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 // selection and no penalty exclusion.  GR_BEAM_KERNEL=stream|ws forces one
 // kernel (ws only where eligible); anything else selects automatically.
 static bool ws_eligible(const Params& P) {
-  return P.K == 0 && !P.partial_only && !(P.mode == kModeProcessed && P.pen && P.T > 0);
+  return P.K == 0 && !(P.mode == kModeProcessed && P.pen && P.T > 0);
 }
 
 static int kernel_choice() {
@@ -1874,7 +1898,7 @@ static int launch_step_kernel(Params& P, DeviceInfo* dev, int dtype_idx, cudaStr
 }
 
 static int launch_merge(const Params& P, DeviceInfo* dev, cudaStream_t stream) {
-  const size_t smem = merge_smem_bytes(P.NB);
+  const size_t smem = merge_smem_bytes(max(P.NB, P.slot_rows));
   if (smem > static_cast<size_t>(dev->smem_optin)) return GR_ERR_UNSUPPORTED;
   if (!dev->merge_attr_set) {
     if (cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dev->smem_optin) !=
@@ -1895,6 +1919,65 @@ static int launch_by_dtype(Params& P, int dtype, DeviceInfo* dev, cudaStream_t s
   }
 }
 
+}  // namespace gr
+
+namespace gr {
+// Checks shared by the entry points, the workspace carve-up and the row
+// metadata launch.  `need_out` / `need_logits`: the call writes the step's
+// outputs / reads the logits.
+static int setup_step(const gr_step_desc* d, const gr_step_io* io, void* workspace, size_t workspace_bytes,
+                      cudaStream_t s, bool need_logits, bool need_out, Params& P, DeviceInfo** dev, float** lse_ws) {
+  if (!d || !io) return GR_ERR_NULL;
+  int v = validate(d);
+  if (v != GR_OK) return v;
+  if ((need_logits && !io->logits) || !io->cum || !io->node || !io->err) return GR_ERR_NULL;
+  if (need_out && (!io->cand_score || !io->cand_token || !io->cand_parent)) return GR_ERR_NULL;
+  if (need_out && (!io->sel_score || !io->sel_token || !io->sel_parent || !io->sel_node)) return GR_ERR_NULL;
+  if (d->num_nodes > 0 && (!io->row_ptr || !io->child_tok || !io->child_node)) return GR_ERR_NULL;
+  if (d->hist_len > 0 && !io->hist_in) return GR_ERR_NULL;
+  const bool pen = io->rep_penalty || io->pres_penalty || io->freq_penalty;
+  if (pen && d->hist_len > kPenTableMax) return GR_ERR_UNSUPPORTED;
+  if (pen && (d->vocab_local + 31) / 32 + 1 > kMaxBitmapWords) return GR_ERR_UNSUPPORTED;
+  if (!workspace) return GR_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u) return GR_ERR_MISALIGNED;
+  size_t need = 0;
+  gr_beam_step_workspace_size(d, &need);
+  if (workspace_bytes < need) return GR_ERR_WORKSPACE;
+  v = device_info(dev);
+  if (v != GR_OK) return v;
+  fill_params(P, d, io);
+  const int R = d->num_requests, NB = d->num_beams;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  size_t o = 0;
+  P.tau = reinterpret_cast<unsigned long long*>(ws + o); o += ws_tau_bytes(R);
+  P.rowcnt = reinterpret_cast<unsigned int*>(ws + o); o += ws_cnt_bytes(R, NB);
+  P.meta = reinterpret_cast<int*>(ws + o); o += ws_meta_bytes(R, NB);
+  P.buf = reinterpret_cast<unsigned long long*>(ws + o); o += align128(size_t(R) * NB * size_t(P.k2) * 8);
+  *lse_ws = reinterpret_cast<float*>(ws + o);
+  const int rows = R * NB;
+  row_meta_kernel<<<(rows + 255) / 256, 256, 0, s>>>(P);
+  if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
+  return GR_OK;
+}
+
+// Vocab-sharded: the rows' global log-sum-exp from every shard's (max, sumexp)
+// partial, combined in shard order (the same value on every rank).
+__global__ void __launch_bounds__(256) lse_combine_kernel(const float2* gathered, int shards, int rows, float* lse_ws,
+                                                          float* lse_out) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  float M = -kInf;
+  for (int k = 0; k < shards; ++k) M = fmaxf(M, gathered[static_cast<size_t>(k) * rows + row].x);
+  float tot = 0.0f;
+  if (M > -kInf)
+    for (int k = 0; k < shards; ++k) {
+      const float2 g = gathered[static_cast<size_t>(k) * rows + row];
+      tot += g.y * fast_exp2((g.x - M) * kLog2e);
+    }
+  const float lse = M + logf(tot);
+  lse_ws[row] = lse;
+  if (lse_out) lse_out[row] = lse;
+}
 }  // namespace gr
 
 using namespace gr;
@@ -1924,47 +2007,20 @@ int32_t gr_beam_step_workspace_size(const gr_step_desc* d, size_t* bytes) {
   if (v != GR_OK) return v;
   const size_t slots = size_t(d->num_requests) * d->num_beams * size_t(2 * d->beam_width);
   *bytes = ws_tau_bytes(d->num_requests) + ws_cnt_bytes(d->num_requests, d->num_beams) +
-           ws_meta_bytes(d->num_requests, d->num_beams) + align128(slots * 8);
+           ws_meta_bytes(d->num_requests, d->num_beams) + align128(slots * 8) +
+           align128(size_t(d->num_requests) * d->num_beams * 4);
   return GR_OK;
 }
 
+
 int32_t gr_beam_step(const gr_step_desc* d, const gr_step_io* io, void* workspace, size_t workspace_bytes,
                      void* stream) {
-  if (!d || !io) return GR_ERR_NULL;
-  int v = validate(d);
-  if (v != GR_OK) return v;
-  if (!io->logits || !io->cum || !io->node || !io->err) return GR_ERR_NULL;
-  if (!io->cand_score || !io->cand_token || !io->cand_parent) return GR_ERR_NULL;
-  if (!io->sel_score || !io->sel_token || !io->sel_parent || !io->sel_node) return GR_ERR_NULL;
-  if (d->num_nodes > 0 && (!io->row_ptr || !io->child_tok || !io->child_node)) return GR_ERR_NULL;
-  if (d->hist_len > 0 && !io->hist_in) return GR_ERR_NULL;
-  const bool pen = io->rep_penalty || io->pres_penalty || io->freq_penalty;
-  if (pen && d->hist_len > kPenTableMax) return GR_ERR_UNSUPPORTED;
-  if (pen && (d->vocab_local + 31) / 32 + 1 > kMaxBitmapWords) return GR_ERR_UNSUPPORTED;
-  if (!workspace) return GR_ERR_NULL;
-  if (reinterpret_cast<uintptr_t>(workspace) & 255u) return GR_ERR_MISALIGNED;
-  size_t need = 0;
-  gr_beam_step_workspace_size(d, &need);
-  if (workspace_bytes < need) return GR_ERR_WORKSPACE;
-  DeviceInfo* dev = nullptr;
-  v = device_info(&dev);
-  if (v != GR_OK) return v;
-
   Params P;
-  fill_params(P, d, io);
-  const int R = d->num_requests;
-  unsigned char* ws = static_cast<unsigned char*>(workspace);
-  P.tau = reinterpret_cast<unsigned long long*>(ws);
-  P.rowcnt = reinterpret_cast<unsigned int*>(ws + ws_tau_bytes(R));
-  P.meta = reinterpret_cast<int*>(ws + ws_tau_bytes(R) + ws_cnt_bytes(R, d->num_beams));
-  P.buf = reinterpret_cast<unsigned long long*>(ws + ws_tau_bytes(R) + ws_cnt_bytes(R, d->num_beams) +
-                                                ws_meta_bytes(R, d->num_beams));
+  DeviceInfo* dev = nullptr;
+  float* lse_ws = nullptr;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  {
-    const int rows = R * d->num_beams;
-    row_meta_kernel<<<(rows + 255) / 256, 256, 0, s>>>(P);
-    if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
-  }
+  int v = setup_step(d, io, workspace, workspace_bytes, s, true, true, P, &dev, &lse_ws);
+  if (v != GR_OK) return v;
   v = launch_by_dtype(P, d->logit_dtype, dev, s);
   if (v != GR_OK) return v;
   return launch_merge(P, dev, s);
@@ -2021,26 +2077,65 @@ int32_t gr_beam_step_noalloc(const gr_step_desc* d, const gr_step_io* io, void* 
   return gr_beam_step(d, io, ptr, kNoAllocScratchBytes, stream);
 }
 
-int32_t gr_lse_partials(const gr_step_desc* d, const void* logits, const float* temperature,
-                        const float* rep_penalty, const float* pres_penalty, const float* freq_penalty,
-                        const int32_t* hist_in, float* partials, int32_t* err, void* stream) {
-  (void)d; (void)logits; (void)temperature; (void)rep_penalty; (void)pres_penalty; (void)freq_penalty;
-  (void)hist_in; (void)partials; (void)err; (void)stream;
-  return GR_ERR_UNSUPPORTED;
+int32_t gr_lse_partials(const gr_step_desc* d, const gr_step_io* io, float* partials, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (!partials) return GR_ERR_NULL;
+  Params P;
+  DeviceInfo* dev = nullptr;
+  float* lse_ws = nullptr;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int v = setup_step(d, io, workspace, workspace_bytes, s, true, false, P, &dev, &lse_ws);
+  if (v != GR_OK) return v;
+  P.partial_only = 1;
+  P.partials = reinterpret_cast<float2*>(partials);
+  P.lse_out = nullptr;
+  P.eos_score = nullptr;
+  return launch_by_dtype(P, d->logit_dtype, dev, s);
 }
 
 int32_t gr_shard_candidates(const gr_step_desc* d, const gr_step_io* io, const float* gathered_partials,
                             int32_t num_shards, uint64_t* shard_keys, void* workspace, size_t workspace_bytes,
                             void* stream) {
-  (void)d; (void)io; (void)gathered_partials; (void)num_shards; (void)shard_keys; (void)workspace;
-  (void)workspace_bytes; (void)stream;
-  return GR_ERR_UNSUPPORTED;
+  if (!gathered_partials || !shard_keys) return GR_ERR_NULL;
+  if (num_shards < 1) return GR_ERR_BAD_DESC;
+  if (d && d->per_beam_k != 0) return GR_ERR_UNSUPPORTED;
+  Params P;
+  DeviceInfo* dev = nullptr;
+  float* lse_ws = nullptr;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int v = setup_step(d, io, workspace, workspace_bytes, s, true, false, P, &dev, &lse_ws);
+  if (v != GR_OK) return v;
+  const int rows = d->num_requests * d->num_beams;
+  lse_combine_kernel<<<(rows + 255) / 256, 256, 0, s>>>(reinterpret_cast<const float2*>(gathered_partials),
+                                                         num_shards, rows, lse_ws, io->lse);
+  if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
+  P.lse_in = lse_ws;
+  P.lse_out = nullptr;
+  v = launch_by_dtype(P, d->logit_dtype, dev, s);
+  if (v != GR_OK) return v;
+  P.keys_out = reinterpret_cast<unsigned long long*>(shard_keys);
+  return launch_merge(P, dev, s);
 }
 
 int32_t gr_merge_candidates(const gr_step_desc* d, const gr_step_io* io, const uint64_t* gathered_keys,
-                            int32_t num_shards, void* stream) {
-  (void)d; (void)io; (void)gathered_keys; (void)num_shards; (void)stream;
-  return GR_ERR_UNSUPPORTED;
+                            int32_t num_shards, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!gathered_keys) return GR_ERR_NULL;
+  if (num_shards < 1 || num_shards > 65535) return GR_ERR_BAD_DESC;
+  if (d && d->per_beam_k != 0) return GR_ERR_UNSUPPORTED;
+  Params P;
+  DeviceInfo* dev = nullptr;
+  float* lse_ws = nullptr;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int v = setup_step(d, io, workspace, workspace_bytes, s, false, true, P, &dev, &lse_ws);
+  if (v != GR_OK) return v;
+  // every shard's [R][2B] list is one slot of the request: slot k of request r
+  // sits at gathered_keys + (k * R + r) * 2B
+  P.buf = const_cast<unsigned long long*>(reinterpret_cast<const unsigned long long*>(gathered_keys));
+  P.rowcnt = nullptr;
+  P.slot_rows = num_shards;
+  P.slot_sr = 1;
+  P.slot_sb = d->num_requests;
+  return launch_merge(P, dev, s);
 }
 
 }  // extern "C"

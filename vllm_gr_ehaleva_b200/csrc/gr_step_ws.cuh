@@ -158,7 +158,7 @@ __device__ void ws_produce(const Params& P, int my_n) {
                           static_cast<uintptr_t>(row) * static_cast<uintptr_t>(P.row_stride) * ES;
       int wlo = 1, whi = 0;
       uint32_t wbytes = 0;
-      if (P.K == 0 && node >= 0 && c1 > c0) {
+      if (P.K == 0 && !P.partial_only && node >= 0 && c1 > c0) {
         const int lo = max(lt - P.voff, 0), hi = min(ht - P.voff, P.VL - 1);
         if (lo <= hi) {
           const uintptr_t body0 = (a + 15) & ~uintptr_t(15);
@@ -186,7 +186,8 @@ __device__ void ws_produce(const Params& P, int my_n) {
     if (lane == 0) {
       mbar_arrive(&W.recfull[slot]);   // release: the record (every lane's word) and the window bounds
       const Geom g = row_geom<ES, ws::kStage>(P, row);
-      for (int ch = 0; ch < g.nchunks; ++ch) {
+      const int nchunks = P.lse_in ? 0 : g.nchunks;   // a given normaliser needs no stream
+      for (int ch = 0; ch < nchunks; ++ch) {
         if (fills >= P.stages &&
             !mbar_wait_bounded(&S.empty[stage], (round - 1u) & 1u, &S.v->abort)) {
           if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
@@ -250,8 +251,9 @@ __device__ void ws_stream_rows(const Params& P, int my_n) {
     const float a = kLog2e * yscale;
     float m = -kInf, s = 0.0f;
     const Geom g = row_geom<ES, ws::kStage>(P, row);
+    const int nchunks = P.lse_in ? 0 : g.nchunks;   // a given normaliser needs no stream
     // head / tail columns outside the 16-byte aligned body (exact online update)
-    {
+    if (!P.lse_in) {
       const int nh = g.head, nt = P.VL - g.tail_start;
       const TL* rowp = reinterpret_cast<const TL*>(g.rowp);
       for (int i = sid; i < nh + nt; i += ws::kStrThreads) {
@@ -266,7 +268,7 @@ __device__ void ws_stream_rows(const Params& P, int my_n) {
     }
     uint64_t sacc0 = pack2(0.0f, 0.0f), sacc1 = pack2(0.0f, 0.0f);
     WS_PROF_T(t_stream);
-    for (int ch = 0; ch < g.nchunks; ++ch) {
+    for (int ch = 0; ch < nchunks; ++ch) {
       WS_PROF_T(t_wait);
       if (!mbar_wait_bounded(&S.full[cstage], cphase, &S.v->abort)) {
         if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
@@ -416,8 +418,16 @@ __device__ void ws_finish_rows(const Params& P, int my_n) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, o);
     float lse = M + logf(tot);
-    // an overflowing or NaN streamed sum (uniform: every finisher has the same tot)
-    if (M > -kInf && !(tot <= 3.0e38f)) lse = ws_exact_row_lse<TL>(P, c, st);
+    if (P.lse_in) {
+      lse = P.lse_in[c.row];   // vocab-sharded phase 2: the global normaliser
+    } else if (M > -kInf && !(tot <= 3.0e38f)) {
+      // an overflowing or NaN streamed sum (uniform: every finisher has the same tot)
+      lse = ws_exact_row_lse<TL>(P, c, st);
+      if (P.partial_only) {
+        M = lse;
+        tot = 1.0f;
+      }
+    }
     WS_PROF_ADD(tid == 0, 14, t_fin);
     if (tid == 0) {
       // the request's running threshold as the producer read it (a stale bound is still valid)
@@ -431,13 +441,22 @@ __device__ void ws_finish_rows(const Params& P, int my_n) {
       S.v->thr_key = c.constrained ? tau_pref : 0ull;
       S.v->thr_y = -kInf;
       W.fin_abort[slot] = S.v->abort;
-      if (P.lse_out) P.lse_out[c.row] = lse;
-      if (P.eos_score) P.eos_score[c.row] = __int_as_float(0x7FC00000);
+      if (P.partial_only) {
+        P.partials[c.row] = make_float2(M, tot);
+      } else {
+        if (P.lse_out) P.lse_out[c.row] = lse;
+        if (P.eos_score) P.eos_score[c.row] = __int_as_float(0x7FC00000);
+      }
     }
     WS_PROF_ADD(tid == 0, 15, t_fin);
     csync();
     WS_PROF_ADD(tid == 0, 7, t_fin);
     if (W.fin_abort[slot]) break;
+    if (P.partial_only) {
+      // vocab-sharded phase 1: the partial is all this row needs
+      if (tid == 0) mbar_arrive(&W.findone[slot]);
+      continue;
+    }
     if (c.constrained) {
       WS_PROF_T(t_cc);
       st.constrained_candidates(c, lse);

@@ -100,16 +100,13 @@ def workspace_size(desc: _lib.StepDesc) -> int:
     return int(n.value)
 
 
-def beam_step(logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor, *, beam_width: int,
-              csr: Optional[tuple] = None, vocab_size: Optional[int] = None, vocab_offset: int = 0,
-              logprobs_mode: str = "raw_logprobs", per_beam_k: int = 0, eos_token_id: Optional[int] = None,
-              hist: Optional[torch.Tensor] = None, temperature=None, repetition_penalty=None,
-              presence_penalty=None, frequency_penalty=None, workspace: Optional[Workspace] = None,
-              stream: Optional[torch.cuda.Stream] = None) -> BeamStepOutput:
-    """One device beam step.  Shapes: logits [R, NB, V_l] (or [R*NB, V_l] with cum/node [R, NB]),
-    cum float32 [R, NB], node int32 [R, NB], hist int32 [R, NB, T], csr = (row_ptr int64,
-    child_tok int32, child_node int32) device tensors."""
-    lib = _lib.load()
+def _prepare(logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor, *, beam_width: int,
+             csr: Optional[tuple] = None, vocab_size: Optional[int] = None, vocab_offset: int = 0,
+             logprobs_mode: str = "raw_logprobs", per_beam_k: int = 0, eos_token_id: Optional[int] = None,
+             hist: Optional[torch.Tensor] = None, temperature=None, repetition_penalty=None,
+             presence_penalty=None, frequency_penalty=None, workspace: Optional[Workspace] = None,
+             stream: Optional[torch.cuda.Stream] = None):
+    """Checks the step inputs and builds (descriptor, io, outputs, workspace, stream)."""
     if not logits.is_cuda:
         raise ValueError("logits must be a CUDA tensor")
     device = logits.device
@@ -180,6 +177,26 @@ def beam_step(logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor, *, be
     nbytes = workspace_size(desc)
     ws = (workspace or Workspace(device)).get(nbytes)
     s = stream if stream is not None else torch.cuda.current_stream(device)
+    # the tensors the io pointers refer to stay alive with the returned tuple
+    keep = (logits, cum, node, hist, row_ptr, child_tok, child_node, temps, reps, press, freqs)
+    return desc, io, out, ws, s, keep
+
+
+def beam_step(logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor, *, beam_width: int,
+              csr: Optional[tuple] = None, vocab_size: Optional[int] = None, vocab_offset: int = 0,
+              logprobs_mode: str = "raw_logprobs", per_beam_k: int = 0, eos_token_id: Optional[int] = None,
+              hist: Optional[torch.Tensor] = None, temperature=None, repetition_penalty=None,
+              presence_penalty=None, frequency_penalty=None, workspace: Optional[Workspace] = None,
+              stream: Optional[torch.cuda.Stream] = None) -> BeamStepOutput:
+    """One device beam step.  Shapes: logits [R, NB, V_l] (or [R*NB, V_l] with cum/node [R, NB]),
+    cum float32 [R, NB], node int32 [R, NB], hist int32 [R, NB, T], csr = (row_ptr int64,
+    child_tok int32, child_node int32) device tensors."""
+    lib = _lib.load()
+    desc, io, out, ws, s, _keep = _prepare(
+        logits, cum, node, beam_width=beam_width, csr=csr, vocab_size=vocab_size, vocab_offset=vocab_offset,
+        logprobs_mode=logprobs_mode, per_beam_k=per_beam_k, eos_token_id=eos_token_id, hist=hist,
+        temperature=temperature, repetition_penalty=repetition_penalty, presence_penalty=presence_penalty,
+        frequency_penalty=frequency_penalty, workspace=workspace, stream=stream)
     st = lib.gr_beam_step(ctypes.byref(desc), ctypes.byref(io), ctypes.c_void_p(ws.data_ptr()),
                           ctypes.c_size_t(ws.numel()), ctypes.c_void_p(s.cuda_stream))
     _lib.check(st, "gr_beam_step")
