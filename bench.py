@@ -289,7 +289,8 @@ def run_ours(args):
                    "l2": "inputs larger than L2 (>= 1.2 GB logits per step), no flush"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": None, "kernel": "gr::fused_step_kernel",
+                     "traffic": None,
+                     "kernel": "gr::fused_step_ws_kernel (timed as the whole step: row_meta + fused + merge)",
                      "algorithmic_bytes_per_launch": int(np.mean(steps_bytes)),
                      "avg_launch_ms": round(avg_launch_ms, 5), "per_level_ms": per_level_ms,
                      "per_level_bytes": [int(b) for b in bytes_cycle]},

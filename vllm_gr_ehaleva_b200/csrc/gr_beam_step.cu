@@ -129,6 +129,7 @@ struct Scalars {
   uint32_t ntab;
   int overflow;
   int abort;
+  int abort_snap;              // the consumers' abort decision at the row end (one value for all)
   int last;
   int discard;
   uint32_t base;
@@ -1307,9 +1308,12 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
       S.red_m[warp] = m;
       S.red_s[warp] = s;
     }
-    if (tid == 0 && !P.partial_only) {
-      S.v->tau_pref = tau_pref;
-      if (c.constrained) S.v->thr_key = tau_pref;      // candidates start from the request bound
+    if (tid == 0) {
+      S.v->abort_snap = S.v->abort;
+      if (!P.partial_only) {
+        S.v->tau_pref = tau_pref;
+        if (c.constrained) S.v->thr_key = tau_pref;      // candidates start from the request bound
+      }
     }
     csync();
     // every thread combines the warp partials (same order, same result everywhere)
@@ -1331,7 +1335,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
       }
     }
     GR_PROF_ADD(2, t_red);
-    if (S.v->abort) goto drain;
+    if (S.v->abort_snap) goto drain;
     GR_PROF_T(t_cand);
 
     if (!P.partial_only) {
