@@ -88,6 +88,7 @@ struct Params {
   int* err;
   // workspace
   unsigned long long* tau;     // [R] running lower bound of the request's 2B-th key
+  unsigned int* row_counter;   // next row to hand out (rows taken dynamically by the CTAs)
   unsigned int* rowcnt;        // [R*NB] keys in each row's slot
   int* meta;                   // [R*NB][kMetaWords] row metadata resolved by row_meta_kernel
   unsigned long long* buf;     // [R*NB][2B] per-row candidate slots
@@ -238,13 +239,16 @@ __device__ __forceinline__ Geom row_geom(const Params& P, int row) {
   return g;
 }
 
-__device__ __forceinline__ int row_of_iter(const Params& P, int it) {
-  // b-major order: the first rows every CTA takes are the requests' best beams,
-  // which raise the per-request thresholds early.
-  const int seq = blockIdx.x + it * gridDim.x;
+// b-major order: the first rows taken are the requests' best beams, which
+// raise the per-request thresholds early.
+__device__ __forceinline__ int row_of_seq(const Params& P, int seq) {
   const int b = seq / P.R;
   const int r = seq - b * P.R;
   return r * P.NB + b;
+}
+
+__device__ __forceinline__ int row_of_iter(const Params& P, int it) {
+  return row_of_seq(P, blockIdx.x + it * gridDim.x);
 }
 
 __device__ __forceinline__ float eff_temperature(const Params& P, int r) {
@@ -469,6 +473,38 @@ struct Step {
     }
   }
 
+  // Ordered integer of window entry i (larger = larger value; 16 significant
+  // bits for 2-byte logits, 32 for f32) and its inverse.
+  __device__ __forceinline__ uint32_t win_ord(int i) const {
+    if constexpr (ES == 4) {
+      return f32_to_ord(reinterpret_cast<const float*>(win())[i]);
+    } else {
+      const uint32_t u = reinterpret_cast<const unsigned short*>(win())[i];
+      return (u & 0x8000u) ? (~u & 0xFFFFu) : (u | 0x8000u);
+    }
+  }
+  __device__ __forceinline__ float ord_value(uint32_t o) const {
+    if constexpr (ES == 4) {
+      return ord_to_f32(o);
+    } else {
+      const uint32_t u = (o & 0x8000u) ? (o & 0x7FFFu) : (~o & 0xFFFFu);
+      if constexpr (std::is_same_v<TL, __nv_bfloat16>) return __uint_as_float(u << 16);
+      else return __half2float(__ushort_as_half(static_cast<unsigned short>(u)));
+    }
+  }
+  // Key of child j at window index i: value first, then the lower child index.
+  __device__ __forceinline__ uint64_t win_value_key(int i, int j) const {
+    if constexpr (ES == 4) {
+      return (static_cast<uint64_t>(win_ord(i)) << 32) | static_cast<uint64_t>(0xFFFFFFFFu - static_cast<uint32_t>(j));
+    } else {
+      return static_cast<uint64_t>((win_ord(i) << 16) | (0xFFFFu - static_cast<uint32_t>(j))) << 32;
+    }
+  }
+  __device__ __forceinline__ float value_of_key(uint64_t k) const {
+    if constexpr (ES == 4) return ord_value(static_cast<uint32_t>(k >> 32));
+    else return ord_value(static_cast<uint32_t>(k >> 48));
+  }
+
   // Score child j (CSR position within the node, token tok) of a catalog row.
   // Its key carries parent * V + j: children are sorted by token, so this
   // orders ties exactly as parent * V + token does, and the merge reads the
@@ -499,11 +535,25 @@ struct Step {
     static_assert(kBatch == kThreads * 8, "dense path: one 8-entry group per thread per batch");
     bool dense_done = false;
     constexpr int kG = 4;   // the one-pass dense scan covers kG * kBatch window entries
-    if (dense_window && d0 + deg <= kG * kBatch && S.v->thr_key != 0ull) {
+    for (int attempt = 0; attempt < 2 && !dense_done && dense_window && d0 + deg <= kG * kBatch; ++attempt) {
+      GR_PROF_T(t_op);
+      if ((S.v->thr_key == 0ull || attempt == 1) && deg > P.k2) {
+        // a weak bound: tighten it with the row's own 2B-th best child value.
+        // Scores are monotone in the value, so every child scoring at least
+        // that value's score is kept, and at least 2B children do.
+        const Cut vc = cta_radix_select([this, d0](int j) { return win_value_key(d0 + j, j); }, deg, P.k2, S.sel);
+        if (threadIdx.x == 0) {
+          const float xt = value_of_key(vc.floor_key());
+          const float st = __fadd_rn(__fadd_rn(c.cum, __fsub_rn(xt, lse)), 0.0f);
+          const uint64_t tk = static_cast<uint64_t>(f32_to_ord(st)) << 32;
+          if (tk > S.v->thr_key) S.v->thr_key = tk;
+        }
+        csync();
+      }
       // one pass over every child with a single reservation per warp; if the key
-      // list overflows (a weak bound), the batched loop below redoes the row
+      // list overflows, the row is redone (tighter bound, or the batched loop)
       const uint64_t thr = S.v->thr_key;
-      const float thr_s = key_score(thr);
+      const float thr_s = thr ? key_score(thr) : -kInf;
       uint32_t pm[kG];
       uint32_t cnt_t = 0;
 #pragma unroll
@@ -524,6 +574,7 @@ struct Step {
         }
         cnt_t += static_cast<uint32_t>(__popc(pm[g]));
       }
+      GR_PROF_ADD(13, t_op);
       uint32_t pos = warp_reserve(cnt_t, &S.v->cnt);
 #pragma unroll
       for (int g = 0; g < kG; ++g) {
@@ -544,7 +595,9 @@ struct Step {
           }
         }
       }
+      GR_PROF_ADD(14, t_op);
       csync();
+      GR_PROF_ADD(15, t_op);
       if (S.v->overflow == 0) {
         dense_done = true;
       } else {
@@ -981,6 +1034,7 @@ __global__ void __launch_bounds__(256) row_meta_kernel(const __grid_constant__ P
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= P.R * P.NB) return;
   if (row % P.NB == 0) P.tau[row / P.NB] = 0ull;   // the request's running bound starts empty
+  if (row == 0) *P.row_counter = 0u;
   int w[kMetaWords];
 #pragma unroll
   for (int i = 0; i < kMetaWords; ++i) w[i] = 0;
@@ -1711,7 +1765,7 @@ static int device_info(DeviceInfo** out) {
 
 // Workspace: tau [R] u64 | row counts [R*NB] u32 | row metadata [R*NB][kMetaWords] i32 |
 // row slots [R*NB][2B] u64.
-static size_t ws_tau_bytes(int R) { return align128(size_t(R) * 8); }
+static size_t ws_tau_bytes(int R) { return align128(size_t(R) * 8 + 8); }   // + the row counter
 static size_t ws_cnt_bytes(int R, int NB) { return align128(size_t(R) * NB * 4); }
 static size_t ws_meta_bytes(int R, int NB) { return align128(size_t(R) * NB * kMetaWords * 4); }
 
@@ -1953,7 +2007,9 @@ static int setup_step(const gr_step_desc* d, const gr_step_io* io, void* workspa
   const int R = d->num_requests, NB = d->num_beams;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   size_t o = 0;
-  P.tau = reinterpret_cast<unsigned long long*>(ws + o); o += ws_tau_bytes(R);
+  P.tau = reinterpret_cast<unsigned long long*>(ws + o);
+  P.row_counter = reinterpret_cast<unsigned int*>(P.tau + R);
+  o += ws_tau_bytes(R);
   P.rowcnt = reinterpret_cast<unsigned int*>(ws + o); o += ws_cnt_bytes(R, NB);
   P.meta = reinterpret_cast<int*>(ws + o); o += ws_meta_bytes(R, NB);
   P.buf = reinterpret_cast<unsigned long long*>(ws + o); o += align128(size_t(R) * NB * size_t(P.k2) * 8);

@@ -97,8 +97,11 @@ __device__ __forceinline__ View view() {
 #endif
 
 // Producer warp: per row, the record and window of its slot, then the body.
+// Rows are taken dynamically: each CTA's producer draws the next sequence
+// number from a global counter (one row ahead), so CTAs with cheap rows take
+// more of them.  A record with row -1 tells the other roles to stop.
 template <typename TL>
-__device__ void ws_produce(const Params& P, int my_n) {
+__device__ void ws_produce(const Params& P) {
   constexpr int ES = sizeof(TL);
   const Smem S = smem_view(P);
   const ws::View W = ws::view();
@@ -110,14 +113,21 @@ __device__ void ws_produce(const Params& P, int my_n) {
   static_assert(kMetaWords == 32, "one record word per producer lane");
   // the next row's record word (lane = word) and its request threshold (lane 0),
   // loaded one row ahead
+  const int total = P.R * P.NB;
+  auto draw = [&]() -> int {
+    int seq = 0;
+    if (lane == 0) seq = static_cast<int>(atomicAdd(P.row_counter, 1u));
+    seq = __shfl_sync(0xFFFFFFFFu, seq, 0);
+    return (seq < total) ? row_of_seq(P, seq) : -1;
+  };
   int meta_word = 0;
   unsigned long long tau_word = 0;
-  int row_next = (my_n > 0) ? row_of_iter(P, 0) : 0;
-  if (my_n > 0) {
+  int row_next = draw();
+  if (row_next >= 0) {
     meta_word = __ldcg(P.meta + static_cast<size_t>(row_next) * kMetaWords + lane);
     if (lane == 0) tau_word = *reinterpret_cast<volatile unsigned long long*>(P.tau + row_next / P.NB);
   }
-  for (int it = 0; it < my_n; ++it) {
+  for (int it = 0;; ++it) {
     const int slot = it & 1;
     const int row = row_next;
     // the slot is free once the finishers are done with row it-2
@@ -135,12 +145,20 @@ __device__ void ws_produce(const Params& P, int my_n) {
         break;
       }
     }
+    if (row < 0) {
+      // no rows left: a stop record for the streaming and row-end warps
+      if (lane == 0) {
+        W.rec(slot)[kMRow] = -1;
+        mbar_arrive(&W.recfull[slot]);
+      }
+      break;
+    }
     const int cur = meta_word;
     const unsigned long long tau_cur = __shfl_sync(0xFFFFFFFFu, tau_word, 0);
     W.rec(slot)[lane] = (lane == kMTauLo) ? static_cast<int>(tau_cur & 0xFFFFFFFFull)
                       : (lane == kMTauHi) ? static_cast<int>(tau_cur >> 32) : cur;
-    if (it + 1 < my_n) {
-      row_next = row_of_iter(P, it + 1);
+    row_next = draw();
+    if (row_next >= 0) {
       meta_word = __ldcg(P.meta + static_cast<size_t>(row_next) * kMetaWords + lane);
       if (lane == 0) tau_word = *reinterpret_cast<volatile unsigned long long*>(P.tau + row_next / P.NB);
     }
@@ -221,7 +239,7 @@ __device__ void ws_produce(const Params& P, int my_n) {
 // the first element it sees; the sum is accumulated without overflow checks
 // (a non-finite total makes the finishers recompute the row exactly).
 template <typename TL>
-__device__ void ws_stream_rows(const Params& P, int my_n) {
+__device__ void ws_stream_rows(const Params& P) {
   const Smem S = smem_view(P);
   const ws::View W = ws::view();
   using Tr = LogitTraits<TL>;
@@ -234,7 +252,8 @@ __device__ void ws_stream_rows(const Params& P, int my_n) {
   long long consumed = 0;
   bool aborted = false;
   WS_PROF_T(t_all);
-  for (int it = 0; it < my_n; ++it) {
+  int rows_done = 0;
+  for (int it = 0;; ++it) {
     const int slot = it & 1;
     WS_PROF_T(t_rf);
     if (!mbar_wait_bounded(&W.recfull[slot], static_cast<uint32_t>(it >> 1) & 1u, &S.v->abort)) {
@@ -247,6 +266,8 @@ __device__ void ws_stream_rows(const Params& P, int my_n) {
       break;
     }
     const int row = W.rec(slot)[kMRow];
+    if (row < 0) break;   // stop record (the same word for every lane)
+    ++rows_done;
     const float yscale = (P.mode == kModeProcessed) ? __int_as_float(W.rec(slot)[kMRteff]) : 1.0f;
     const float a = kLog2e * yscale;
     float m = -kInf, s = 0.0f;
@@ -320,7 +341,7 @@ __device__ void ws_stream_rows(const Params& P, int my_n) {
   }
   WS_PROF_ADD(sid == 0, 11, t_all);
 #ifdef GR_PHASE_PROFILE
-  if (sid == 0) S.v->prof[10] += my_n;
+  if (sid == 0) S.v->prof[10] += rows_done;
 #endif
   if (aborted && sid == 0) {
     // wait (bounded) for the producer to stop and for its copies still in flight
@@ -370,7 +391,7 @@ __device__ float ws_exact_row_lse(const Params& P, const RowCtx& c, const Step<T
 
 // Finishers: row end of every row, one row behind the streamers.
 template <typename TL>
-__device__ void ws_finish_rows(const Params& P, int my_n) {
+__device__ void ws_finish_rows(const Params& P) {
   const Smem S = smem_view(P);
   const ws::View W = ws::view();
   Step<TL> st(P);
@@ -378,11 +399,14 @@ __device__ void ws_finish_rows(const Params& P, int my_n) {
   constexpr int EPV = Tr::kPerVec;
   constexpr int kSubVecs = kBatch / EPV;
   const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
-  for (int it = 0; it < my_n; ++it) {
+  for (int it = 0;; ++it) {
     const int slot = it & 1;
     const uint32_t par = static_cast<uint32_t>(it >> 1) & 1u;
     WS_PROF_T(t_rd);
-    bool ok = mbar_wait_bounded(&W.rowdone[slot], par, &S.v->abort);
+    bool ok = mbar_wait_bounded(&W.recfull[slot], par, &S.v->abort);
+    // the stop record ends the loop for every finisher (all read the same word)
+    if (ok && W.rec(slot)[kMRow] < 0) break;
+    ok = ok && mbar_wait_bounded(&W.rowdone[slot], par, &S.v->abort);
     ok = ok && mbar_wait_bounded(&W.winfull[slot], par, &S.v->abort);
     if (!ok) {
       if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
@@ -405,7 +429,6 @@ __device__ void ws_finish_rows(const Params& P, int my_n) {
     }
     st.rec = rec;
     st.win_off = slot ? ws::kWin1Off : 0;
-    WS_PROF_ADD(tid == 0, 13, t_fin);
     // normaliser: lane w of every finisher warp takes streamer partial w; the
     // same shuffle tree in every warp gives every thread the same value
     static_assert(ws::kStrWarps <= 32, "one partial per lane");
@@ -428,7 +451,6 @@ __device__ void ws_finish_rows(const Params& P, int my_n) {
         tot = 1.0f;
       }
     }
-    WS_PROF_ADD(tid == 0, 14, t_fin);
     if (tid == 0) {
       // the request's running threshold as the producer read it (a stale bound is still valid)
       uint64_t tau_pref = static_cast<uint64_t>(static_cast<uint32_t>(rec[kMTauLo])) |
@@ -448,7 +470,6 @@ __device__ void ws_finish_rows(const Params& P, int my_n) {
         if (P.eos_score) P.eos_score[c.row] = __int_as_float(0x7FC00000);
       }
     }
-    WS_PROF_ADD(tid == 0, 15, t_fin);
     csync();
     WS_PROF_ADD(tid == 0, 7, t_fin);
     if (W.fin_abort[slot]) break;
@@ -527,10 +548,6 @@ __global__ void __launch_bounds__(ws::kBlockWs, 1) fused_step_ws_kernel(const __
   const Smem S = smem_view(P);
   const ws::View W = ws::view();
   const int tid = threadIdx.x, warp = warp_id();
-  const int total = P.R * P.NB;
-  const int my_n = (static_cast<int>(blockIdx.x) < total)
-                       ? (total - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
-                       : 0;
   if (tid == 0) {
     for (int s = 0; s < P.stages; ++s) {
       mbar_init(&S.full[s], 1);
@@ -552,11 +569,11 @@ __global__ void __launch_bounds__(ws::kBlockWs, 1) fused_step_ws_kernel(const __
   pdl_trigger();
   __syncthreads();
   if (warp == ws::kProdWarp) {
-    ws_produce<TL>(P, my_n);
+    ws_produce<TL>(P);
   } else if (warp >= ws::kFinWarps) {
-    ws_stream_rows<TL>(P, my_n);
+    ws_stream_rows<TL>(P);
   } else {
-    ws_finish_rows<TL>(P, my_n);
+    ws_finish_rows<TL>(P);
   }
 #ifdef GR_PHASE_PROFILE
   __syncthreads();
