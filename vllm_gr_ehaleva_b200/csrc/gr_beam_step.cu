@@ -554,6 +554,10 @@ struct Step {
       // list overflows, the row is redone (tighter bound, or the batched loop)
       const uint64_t thr = S.v->thr_key;
       const float thr_s = thr ? key_score(thr) : -kInf;
+      // dense children score as the window value (no temperature, no table):
+      // the key arithmetic runs branch-free for all of them; EOS keeps a -inf
+      // score and records its completion score
+      const int eos_j = (P.eos >= 0) ? P.eos - c.lo_tok : -1;
       uint32_t pm[kG];
       uint32_t cnt_t = 0;
 #pragma unroll
@@ -564,11 +568,23 @@ struct Step {
         if (w0 < d0 + deg) {
           float x[8];
           win_load8(w0, x);
+          float xm = x[0];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float sc = __fadd_rn(c.cum, __fsub_rn(x[i], lse));
-            if (i0 + i >= 0 && i0 + i < deg && (sc >= thr_s || c.lo_tok + i0 + i == P.eos)) {
-              if (child_key(c, c.lo_tok + i0 + i, i0 + i, x[i], lse, fb) >= thr) pm[g] |= 1u << i;
+          for (int i = 1; i < 8; ++i) xm = fmaxf(xm, x[i]);
+          // scores are monotone in the value: a group whose best score misses the
+          // bound has no candidate (only its EOS child, if any, needs a look)
+          const bool eos_here = eos_j >= i0 && eos_j < i0 + 8;
+          if (eos_here || !(__fadd_rn(c.cum, __fsub_rn(xm, lse)) < thr_s)) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int j = i0 + i;
+              const bool in = (j >= 0) && (j < deg);
+              float sc = __fadd_rn(c.cum, __fsub_rn(x[i], lse));
+              if (in && j == eos_j) {
+                if (P.eos_score) P.eos_score[c.row] = sc;
+                sc = -kInf;
+              }
+              if (in && make_key(sc, fb + static_cast<uint32_t>(j)) >= thr) pm[g] |= 1u << i;
             }
           }
         }
@@ -586,8 +602,10 @@ struct Step {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             if ((pm[g] >> i) & 1u) {
+              const int j = i0 + i;
+              const float sc = (j == eos_j) ? -kInf : __fadd_rn(c.cum, __fsub_rn(x[i], lse));
               if (pos < static_cast<uint32_t>(kKeyCap))
-                S.keys[pos] = child_key(c, c.lo_tok + i0 + i, i0 + i, x[i], lse, fb);
+                S.keys[pos] = make_key(sc, fb + static_cast<uint32_t>(j));
               else
                 S.v->overflow = 1;
               ++pos;
