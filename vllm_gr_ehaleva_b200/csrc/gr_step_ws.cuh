@@ -37,51 +37,55 @@ constexpr int kVecPerThread = 4;
 constexpr int kStage = kStrThreads * kVecPerThread * 16;   // 4 vectors per streaming thread per stage
 constexpr int kMaxStagesWs = kMaxStages;          // full/empty barriers live in the common layout
 
+// Rows rotate through kSlots slots (record, child window, partials), so the
+// producer can run two rows ahead of the row-end warps.
+constexpr int kSlots = 3;
+
 // Pieces after the common fixed layout (the penalty pieces are never used here).
-constexpr size_t kOffWin1 = kOffVar;                                   // slot 1's child window
-constexpr size_t kOffRec = kOffWin1 + align128(size_t(kWinBytes));     // records [2][kMetaWords]
-constexpr size_t kOffPart = kOffRec + align128(2 * kMetaWords * 4);    // partial m, s [2][kStrWarps]
-constexpr size_t kOffRowBars = kOffPart + align128(2 * 2 * kStrWarps * 4);
-constexpr size_t kOffFlags = kOffRowBars + align128(8 * 8);
+constexpr size_t kOffWin1 = kOffVar;                                      // slots 1.. child windows
+constexpr size_t kOffRec = kOffWin1 + (kSlots - 1) * align128(size_t(kWinBytes));   // records [kSlots][kMetaWords]
+constexpr size_t kOffPart = kOffRec + align128(kSlots * kMetaWords * 4);  // partial m, s [2][kSlots][kStrWarps]
+constexpr size_t kOffRowBars = kOffPart + align128(2 * kSlots * kStrWarps * 4);
+constexpr size_t kOffFlags = kOffRowBars + align128(4 * kSlots * 8);
 constexpr size_t kOffRing = kOffFlags + 128;
 
 __host__ __device__ constexpr size_t smem_bytes(int stages) { return kOffRing + size_t(stages) * kStage; }
 
-// Window byte offset of slot 1 relative to the common window (slot 0).
-constexpr int kWin1Off = static_cast<int>(kOffWin1 - kOffWin);
+// Window byte offset of a slot relative to the common window (slot 0).
+__host__ __device__ constexpr int win_off(int slot) {
+  return slot ? static_cast<int>(kOffWin1 - kOffWin) + (slot - 1) * static_cast<int>(align128(size_t(kWinBytes))) : 0;
+}
 
 struct View {
-  int* rec0;           // records [2][kMetaWords]
-  float* part_m0;      // partial maxima [2][kStrWarps]
-  float* part_s0;      // partial sums [2][kStrWarps]
-  uint64_t* recfull;   // [2] producer -> streamers and finishers: record and window bounds written
-  uint64_t* winfull;   // [2] producer (bulk copy) -> finishers: window landed
-  uint64_t* rowdone;   // [2] streamers -> finishers (one arrival per streaming warp)
-  uint64_t* findone;   // [2] finishers -> producer: slot free
-  volatile int* fin_abort;   // [2] finishers' per-row abort decision
-  int* win_lo;         // [2] first local column of the slot's window
-  int* win_hi;         // [2] last local column of the slot's window (win_lo > win_hi: none)
+  int* rec0;           // records [kSlots][kMetaWords]
+  float* part_m0;      // partial maxima [kSlots][kStrWarps]
+  float* part_s0;      // partial sums [kSlots][kStrWarps]
+  uint64_t* recfull;   // [kSlots] producer -> streamers and finishers: record and window bounds written
+  uint64_t* winfull;   // [kSlots] producer (bulk copy) -> finishers: window landed
+  uint64_t* rowdone;   // [kSlots] streamers -> finishers (one arrival per streaming warp)
+  uint64_t* findone;   // [kSlots] finishers -> producer: slot free
+  volatile int* fin_abort;   // [kSlots] finishers' per-row abort decision
+  int* win_lo;         // [kSlots] first local column of the slot's window
+  int* win_hi;         // [kSlots] last local column of the slot's window (win_lo > win_hi: none)
   unsigned char* ring;
   __device__ __forceinline__ int* rec(int slot) const { return rec0 + slot * kMetaWords; }
   __device__ __forceinline__ float* part_m(int slot) const { return part_m0 + slot * kStrWarps; }
   __device__ __forceinline__ float* part_s(int slot) const { return part_s0 + slot * kStrWarps; }
-  __device__ __forceinline__ unsigned char* win(int slot) const {
-    return g_smem + (slot ? kOffWin1 : kOffWin);
-  }
+  __device__ __forceinline__ unsigned char* win(int slot) const { return g_smem + kOffWin + win_off(slot); }
 };
 
 __device__ __forceinline__ View view() {
   View W;
   W.rec0 = reinterpret_cast<int*>(g_smem + kOffRec);
   W.part_m0 = reinterpret_cast<float*>(g_smem + kOffPart);
-  W.part_s0 = W.part_m0 + 2 * kStrWarps;
+  W.part_s0 = W.part_m0 + kSlots * kStrWarps;
   W.recfull = reinterpret_cast<uint64_t*>(g_smem + kOffRowBars);
-  W.winfull = W.recfull + 2;
-  W.rowdone = W.recfull + 4;
-  W.findone = W.recfull + 6;
+  W.winfull = W.recfull + kSlots;
+  W.rowdone = W.recfull + 2 * kSlots;
+  W.findone = W.recfull + 3 * kSlots;
   W.fin_abort = reinterpret_cast<volatile int*>(g_smem + kOffFlags);
-  W.win_lo = reinterpret_cast<int*>(g_smem + kOffFlags) + 2;
-  W.win_hi = W.win_lo + 2;
+  W.win_lo = reinterpret_cast<int*>(g_smem + kOffFlags) + kSlots;
+  W.win_hi = W.win_lo + kSlots;
   W.ring = g_smem + kOffRing;
   return W;
 }
@@ -128,14 +132,14 @@ __device__ void ws_produce(const Params& P) {
     if (lane == 0) tau_word = *reinterpret_cast<volatile unsigned long long*>(P.tau + row_next / P.NB);
   }
   for (int it = 0;; ++it) {
-    const int slot = it & 1;
+    const int slot = it % ws::kSlots;
     const int row = row_next;
-    // the slot is free once the finishers are done with row it-2
-    if (it >= 2) {
+    // the slot is free once the finishers are done with row it - kSlots
+    if (it >= ws::kSlots) {
       WS_PROF_T(t_fd);
       int good = 1;
       if (lane == 0)
-        good = mbar_wait_bounded(&W.findone[slot], static_cast<uint32_t>((it - 2) >> 1) & 1u, &S.v->abort) ? 1 : 0;
+        good = mbar_wait_bounded(&W.findone[slot], static_cast<uint32_t>(it / ws::kSlots - 1) & 1u, &S.v->abort) ? 1 : 0;
       WS_PROF_ADD(lane == 0, 6, t_fd);
       if (!__shfl_sync(0xFFFFFFFFu, good, 0)) {
         if (lane == 0) {
@@ -254,9 +258,9 @@ __device__ void ws_stream_rows(const Params& P) {
   WS_PROF_T(t_all);
   int rows_done = 0;
   for (int it = 0;; ++it) {
-    const int slot = it & 1;
+    const int slot = it % ws::kSlots;
     WS_PROF_T(t_rf);
-    if (!mbar_wait_bounded(&W.recfull[slot], static_cast<uint32_t>(it >> 1) & 1u, &S.v->abort)) {
+    if (!mbar_wait_bounded(&W.recfull[slot], static_cast<uint32_t>(it / ws::kSlots) & 1u, &S.v->abort)) {
       if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
       S.v->abort = 1;
     }
@@ -400,8 +404,8 @@ __device__ void ws_finish_rows(const Params& P) {
   constexpr int kSubVecs = kBatch / EPV;
   const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
   for (int it = 0;; ++it) {
-    const int slot = it & 1;
-    const uint32_t par = static_cast<uint32_t>(it >> 1) & 1u;
+    const int slot = it % ws::kSlots;
+    const uint32_t par = static_cast<uint32_t>(it / ws::kSlots) & 1u;
     WS_PROF_T(t_rd);
     bool ok = mbar_wait_bounded(&W.recfull[slot], par, &S.v->abort);
     // the stop record ends the loop for every finisher (all read the same word)
@@ -428,7 +432,7 @@ __device__ void ws_finish_rows(const Params& P) {
       c.whi = W.win_hi[slot];
     }
     st.rec = rec;
-    st.win_off = slot ? ws::kWin1Off : 0;
+    st.win_off = ws::win_off(slot);
     // normaliser: lane w of every finisher warp takes streamer partial w; the
     // same shuffle tree in every warp gives every thread the same value
     static_assert(ws::kStrWarps <= 32, "one partial per lane");
@@ -553,7 +557,7 @@ __global__ void __launch_bounds__(ws::kBlockWs, 1) fused_step_ws_kernel(const __
       mbar_init(&S.full[s], 1);
       mbar_init(&S.empty[s], ws::kStrWarps);
     }
-    for (int q = 0; q < 2; ++q) {
+    for (int q = 0; q < ws::kSlots; ++q) {
       mbar_init(&W.recfull[q], 1);
       mbar_init(&W.winfull[q], 1);
       mbar_init(&W.rowdone[q], ws::kStrWarps);
