@@ -536,7 +536,6 @@ struct Step {
     bool dense_done = false;
     constexpr int kG = 4;   // the one-pass dense scan covers kG * kBatch window entries
     for (int attempt = 0; attempt < 2 && !dense_done && dense_window && d0 + deg <= kG * kBatch; ++attempt) {
-      GR_PROF_T(t_op);
       if ((S.v->thr_key == 0ull || attempt == 1) && deg > P.k2) {
         // a weak bound: tighten it with the row's own 2B-th best child value.
         // Scores are monotone in the value, so every child scoring at least
@@ -590,7 +589,6 @@ struct Step {
         }
         cnt_t += static_cast<uint32_t>(__popc(pm[g]));
       }
-      GR_PROF_ADD(13, t_op);
       uint32_t pos = warp_reserve(cnt_t, &S.v->cnt);
 #pragma unroll
       for (int g = 0; g < kG; ++g) {
@@ -613,9 +611,7 @@ struct Step {
           }
         }
       }
-      GR_PROF_ADD(14, t_op);
       csync();
-      GR_PROF_ADD(15, t_op);
       if (S.v->overflow == 0) {
         dense_done = true;
       } else {
@@ -964,6 +960,20 @@ __device__ __forceinline__ void fold(uint64_t& a0, uint64_t& a1, float& s) {
 template <typename TL>
 struct FastSum;
 
+// Word groups of a 16-byte vector (of 4) whose exponentials use the FMA-pipe
+// polynomial instead of the MUFU unit (2-byte logits only, where the MUFU rate
+// is the tighter limit: 8 exponentials per 16 bytes).
+#ifndef GR_POLY_EXP_GROUPS
+#define GR_POLY_EXP_GROUPS 0
+#endif
+
+__device__ __forceinline__ uint64_t exp2_pair(uint64_t t2, bool poly) {
+  if (poly) return poly_exp2x2(t2);
+  float t0, t1;
+  unpack2(t2, t0, t1);
+  return pack2(fast_exp2(t0), fast_exp2(t1));
+}
+
 template <>
 struct FastSum<__nv_bfloat16> {
   static constexpr int kWords = 4;   // 32-bit words per 16-byte vector
@@ -972,9 +982,7 @@ struct FastSum<__nv_bfloat16> {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint64_t x2 = pack2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
-      float t0, t1;
-      unpack2(ffma2(x2, A2, C2), t0, t1);
-      const uint64_t e2 = pack2(fast_exp2(t0), fast_exp2(t1));
+      const uint64_t e2 = exp2_pair(ffma2(x2, A2, C2), i >= 4 - GR_POLY_EXP_GROUPS);
       if (i & 1) p1 = fadd2(p1, e2); else p0 = fadd2(p0, e2);
     }
   }
@@ -987,9 +995,7 @@ struct FastSum<__half> {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-      float t0, t1;
-      unpack2(ffma2(pack2(f.x, f.y), A2, C2), t0, t1);
-      const uint64_t e2 = pack2(fast_exp2(t0), fast_exp2(t1));
+      const uint64_t e2 = exp2_pair(ffma2(pack2(f.x, f.y), A2, C2), i >= 4 - GR_POLY_EXP_GROUPS);
       if (i & 1) p1 = fadd2(p1, e2); else p0 = fadd2(p0, e2);
     }
   }

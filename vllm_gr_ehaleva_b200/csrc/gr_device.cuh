@@ -165,6 +165,44 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
   return d;
 }
 
+// 2^t for a pair of floats on the FMA pipe (so that part of a row's
+// exponentials leave the MUFU unit): Cody-Waite style range reduction
+// t = n + f, n = round(t), |f| <= 1/2, then a degree-5 polynomial for 2^f
+// (coefficients fitted here by iteratively reweighted least squares for
+// minimax relative error on [-1/2, 1/2]; max relative error 2.4e-7 in float32
+// Horner form) and n added to the exponent field.  t is clamped to
+// [-125, 128]: results below 2^-125 are negligible next to the sums they enter,
+// and t >= 128 yields inf or NaN, as the hardware exp2 overflows.  NaN in gives
+// NaN out.
+constexpr float kP0 = 1.0000001192092896f, kP1 = 0.6931469440460205f, kP2 = 0.24022120237350464f;
+constexpr float kP3 = 0.05550713092088699f, kP4 = 0.009675541892647743f, kP5 = 0.0013276472454890609f;
+
+__device__ __forceinline__ uint64_t poly_exp2x2(uint64_t t2) {
+  float t0, t1;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(t0), "=f"(t1) : "l"(t2));
+  asm("max.NaN.f32 %0, %0, 0fC2FA0000;" : "+f"(t0));   // -125
+  asm("max.NaN.f32 %0, %0, 0fC2FA0000;" : "+f"(t1));
+  asm("min.NaN.f32 %0, %0, 0f43000000;" : "+f"(t0));   // 128
+  asm("min.NaN.f32 %0, %0, 0f43000000;" : "+f"(t1));
+  uint64_t tt;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(tt) : "f"(t0), "f"(t1));
+  const uint64_t r = fadd2(tt, pack2(12582912.0f, 12582912.0f));   // 1.5 * 2^23: round to integer
+  const uint64_t n = fadd2(r, pack2(-12582912.0f, -12582912.0f));
+  const uint64_t f = ffma2(n, pack2(-1.0f, -1.0f), tt);              // t - n, exact
+  uint64_t p = ffma2(pack2(kP5, kP5), f, pack2(kP4, kP4));
+  p = ffma2(p, f, pack2(kP3, kP3));
+  p = ffma2(p, f, pack2(kP2, kP2));
+  p = ffma2(p, f, pack2(kP1, kP1));
+  p = ffma2(p, f, pack2(kP0, kP0));
+  float r0, r1, p0, p1;
+  unpack2(r, r0, r1);
+  unpack2(p, p0, p1);
+  // the low bits of r hold n: n << 23 added to the exponent of 2^f
+  const float e0 = __uint_as_float(__float_as_uint(r0) * 0x800000u + __float_as_uint(p0));
+  const float e1 = __uint_as_float(__float_as_uint(r1) * 0x800000u + __float_as_uint(p1));
+  return pack2(e0, e1);
+}
+
 // ---------------------------------------------------------------- keys
 __device__ __forceinline__ uint32_t f32_to_ord(float f) {
   const uint32_t u = __float_as_uint(f);

@@ -292,6 +292,7 @@ __device__ void ws_stream_rows(const Params& P) {
       }
     }
     uint64_t sacc0 = pack2(0.0f, 0.0f), sacc1 = pack2(0.0f, 0.0f);
+    WS_PROF_ADD(sid == 0, 14, t_rf);
     WS_PROF_T(t_stream);
     for (int ch = 0; ch < nchunks; ++ch) {
       WS_PROF_T(t_wait);
@@ -327,21 +328,23 @@ __device__ void ws_stream_rows(const Params& P) {
         if (sid + j * ws::kStrThreads < nvec) FastSum<TL>::add(vv[j], A2, C2, sacc0, sacc1);
     }
     WS_PROF_ADD(sid == 0, 0, t_stream);
+    WS_PROF_T(t_end);
     fold(sacc0, sacc1, s);
-    // warp partial of (m, s); the finishers combine the kStrWarps partials
+    // warp partial of (m, s): the warp maximum, then every lane's sum rescaled
+    // to it once and added up; the finishers combine the kStrWarps partials
+    float M = m;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float m2 = __shfl_xor_sync(0xFFFFFFFFu, m, o);
-      const float s2 = __shfl_xor_sync(0xFFFFFFFFu, s, o);
-      const float M = fmaxf(m, m2);
-      s = (M == -kInf) ? 0.0f : s * fast_exp2((m - M) * kLog2e) + s2 * fast_exp2((m2 - M) * kLog2e);
-      m = M;
-    }
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+    s = (m == -kInf) ? 0.0f : s * fast_exp2((m - M) * kLog2e);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+    m = M;
     if (lane == 0) {
       W.part_m(slot)[swarp] = m;
       W.part_s(slot)[swarp] = s;
       mbar_arrive(&W.rowdone[slot]);   // release: the warp's partial
     }
+    WS_PROF_ADD(sid == 0, 13, t_end);
   }
   WS_PROF_ADD(sid == 0, 11, t_all);
 #ifdef GR_PHASE_PROFILE
