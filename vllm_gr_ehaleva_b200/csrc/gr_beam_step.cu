@@ -102,9 +102,12 @@ struct Params {
   float2* partials;
   const float* lse_in;            // vocab-sharded phase 2: the rows' global normaliser (no streaming)
   unsigned long long* keys_out;   // merge writes the sorted top-2B keys [R][2B] (zero padded) instead
-  // merge input grid: request r's slot s sits at buf + (r * slot_sr + s * slot_sb) * 2B
+  // merge input grid: request r's slot s sits at buf + (r * slot_sr + s * slot_sb) * 2B and
+  // holds up to slot_cap keys.  The step's own lists are one slot per request
+  // (slot_rows 1, the rows' keys appended at rowcnt[r * NB]).
   int slot_rows;
   long long slot_sr, slot_sb;
+  int slot_cap;
 };
 
 // Shared-memory layout (dynamic shared memory).  Every piece but the ring sits
@@ -897,9 +900,13 @@ struct Step {
       if (threadIdx.x == 0) atomicOr(P.err, GR_DEVERR_OVERFLOW);
       n = P.k2;
     }
-    unsigned long long* dst = P.buf + static_cast<size_t>(c.row) * static_cast<size_t>(P.k2);
-    for (int i = threadIdx.x; i < n; i += kThreads) dst[i] = S.keys[i];
-    if (threadIdx.x == 0) P.rowcnt[c.row] = static_cast<unsigned>(n);
+    // append to the request's candidate list (one reservation per row); the
+    // merge reads it right after this kernel: keep it in L2 ahead of the stream
+    if (threadIdx.x == 0) S.v->base = (n > 0) ? atomicAdd(P.rowcnt + static_cast<size_t>(c.r) * P.NB, static_cast<unsigned>(n)) : 0u;
+    csync();
+    unsigned long long* dst = P.buf + static_cast<size_t>(c.r) * P.NB * static_cast<size_t>(P.k2) + S.v->base;
+    const uint64_t keep = l2_policy_evict_last();
+    for (int i = threadIdx.x; i < n; i += kThreads) st_keep_u64(dst + i, S.keys[i], keep);
   }
 };
 
@@ -1057,7 +1064,10 @@ __global__ void __launch_bounds__(256) row_meta_kernel(const __grid_constant__ P
   pdl_trigger();   // the step kernel may start its prologue; it waits for this grid before reading
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= P.R * P.NB) return;
-  if (row % P.NB == 0) P.tau[row / P.NB] = 0ull;   // the request's running bound starts empty
+  if (row % P.NB == 0) {
+    P.tau[row / P.NB] = 0ull;     // the request's running bound starts empty
+    P.rowcnt[row] = 0u;           // and its candidate list
+  }
   if (row == 0) *P.row_counter = 0u;
   int w[kMetaWords];
 #pragma unroll
@@ -1090,7 +1100,8 @@ __global__ void __launch_bounds__(256) row_meta_kernel(const __grid_constant__ P
   }
   int4* dst = reinterpret_cast<int4*>(P.meta + static_cast<size_t>(row) * kMetaWords);
 #pragma unroll
-  for (int i = 0; i < kMetaWords / 4; ++i) dst[i] = make_int4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  const uint64_t keep = l2_policy_evict_last();   // read by the step and merge kernels
+  for (int i = 0; i < kMetaWords / 4; ++i) st_keep_v4(dst + i, make_int4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]), keep);
 }
 
 template <typename TL>
@@ -1554,8 +1565,8 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
   const int b0 = min(tid * per, S), b1 = min(b0 + per, S);
   uint32_t local = 0;
   for (int b = b0; b < b1; ++b) {
-    const uint32_t c = P.rowcnt ? min(__ldcg(P.rowcnt + static_cast<size_t>(r) * NB + b), static_cast<unsigned>(k2))
-                                : static_cast<uint32_t>(k2);
+    const uint32_t c = P.rowcnt ? min(__ldcg(P.rowcnt + static_cast<size_t>(r) * NB + b), static_cast<unsigned>(P.slot_cap))
+                                : static_cast<uint32_t>(P.slot_cap);
     M.rc[b] = c;
     local += c;
   }
@@ -1604,9 +1615,11 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
   if (n_all <= kMergeCap) {
     // row of every gathered index (one warp per row), then a flat gather with
     // kU independent loads per thread in flight
-    for (int b = warp; b < S; b += kWarps)
-      for (uint32_t j = lane; j < rc[b]; j += 32) M.row_of[prefix[b] + j] = static_cast<uint16_t>(b);
-    csync();
+    if (S > 1) {
+      for (int b = warp; b < S; b += kWarps)
+        for (uint32_t j = lane; j < rc[b]; j += 32) M.row_of[prefix[b] + j] = static_cast<uint16_t>(b);
+      csync();
+    }
     constexpr int kU = 16;
     for (int base0 = 0; base0 < n_all; base0 += kThreads * kU) {
       // addresses first, then every load, then the uses: no load waits for another
@@ -1614,7 +1627,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
         const int i = min(base0 + u * kThreads + tid, n_all - 1);
-        const int b = M.row_of[i];
+        const int b = (S > 1) ? M.row_of[i] : 0;
         src[u] = slots + static_cast<size_t>(b) * slot_step + (static_cast<uint32_t>(i) - prefix[b]);
       }
       uint64_t kv[kU];
@@ -1861,9 +1874,10 @@ static void fill_params(Params& P, const gr_step_desc* d, const gr_step_io* io) 
   P.partials = nullptr;
   P.lse_in = nullptr;
   P.keys_out = nullptr;
-  P.slot_rows = d->num_beams;
+  P.slot_rows = 1;
   P.slot_sr = d->num_beams;
   P.slot_sb = 1;
+  P.slot_cap = d->num_beams * 2 * d->beam_width;
 }
 
 // Two CTAs per SM when at least three ring stages fit beside the fixed
@@ -2219,6 +2233,7 @@ int32_t gr_merge_candidates(const gr_step_desc* d, const gr_step_io* io, const u
   P.slot_rows = num_shards;
   P.slot_sr = 1;
   P.slot_sb = d->num_requests;
+  P.slot_cap = 2 * d->beam_width;
   return launch_merge(P, dev, s);
 }
 

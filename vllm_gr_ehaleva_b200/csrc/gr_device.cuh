@@ -130,6 +130,25 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
       : "memory");
 }
 
+// L2 policy that keeps lines resident ahead of streamed (evict-first) data:
+// for the small per-step buffers the next kernel reads back.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void st_keep_u64(unsigned long long* p, unsigned long long v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.u64 [%0], %1, %2;" ::"l"(p), "l"(v), "l"(pol) : "memory");
+}
+__device__ __forceinline__ void st_keep_u32(unsigned* p, unsigned v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.u32 [%0], %1, %2;" ::"l"(p), "r"(v), "l"(pol) : "memory");
+}
+__device__ __forceinline__ void st_keep_v4(int4* p, int4 v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v4.s32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w), "l"(pol)
+               : "memory");
+}
+
 // As bulk_copy_g2s with the default L2 policy (the bytes are read again soon).
 __device__ __forceinline__ void bulk_copy_g2s_keep(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
