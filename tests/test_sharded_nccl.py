@@ -1,0 +1,80 @@
+"""Vocab-sharded step across real GPUs: one process per GPU, NCCL all-gathers
+(torch_all_gather), each rank holding a column slice of the logits.  Every
+rank's outputs must equal the oracle's full-vocabulary step (bit-exact given
+the combined lse).  Needs two GPUs; skipped otherwise."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    try:
+        import datetime
+        import sys
+        import torch
+        import torch.distributed as dist
+        sys.path.insert(0, os.path.dirname(__file__))
+        from helpers import Case, make_logits, small_catalog, to_device_logits, OUT_KEYS
+        from vllm_gr_ehaleva_b200.sharded import sharded_beam_step, torch_all_gather
+        from vllm_gr_ehaleva_b200.synthetic import initial_cum
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        cat = small_catalog()
+        R, NB, B, V = 2, 16, 16, 8192
+        case = Case(logits32=make_logits(R, NB, V, 4.0, 21, "bf16"), dtype="bf16", cum=initial_cum(R, NB),
+                    node=np.full((R, NB), cat.start_node, np.int32), beam_width=B, vocab_size=V, csr=cat.csr,
+                    hist=np.full((R, NB, 1), cat.sid_begin, np.int32))
+        dev = torch.device("cuda", rank)
+        VL = V // world
+        local = to_device_logits(case, dev)[:, rank * VL:(rank + 1) * VL]
+        csr = tuple(torch.from_numpy(a).to(dev) for a in (cat.csr.row_ptr, cat.csr.child_tok, cat.csr.child_node))
+        out = sharded_beam_step(local, torch.from_numpy(case.cum).to(dev), torch.from_numpy(case.node).to(dev),
+                                all_gather=torch_all_gather(), beam_width=B, vocab_size=V, vocab_offset=rank * VL,
+                                csr=csr, hist=torch.from_numpy(case.hist).to(dev))
+        torch.cuda.synchronize()
+        res = {k: getattr(out, k).cpu().numpy() for k in OUT_KEYS}
+        res["err"] = int(out.err.item())
+        q.put((rank, res))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, {"error": repr(e)}))
+
+
+def test_sharded_step_two_gpus_nccl():
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from helpers import Case, assert_step_parity, make_logits, small_catalog
+    from vllm_gr_ehaleva_b200.synthetic import initial_cum
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    cat = small_catalog()
+    R, NB, B, V = 2, 16, 16, 8192
+    case = Case(logits32=make_logits(R, NB, V, 4.0, 21, "bf16"), dtype="bf16", cum=initial_cum(R, NB),
+                node=np.full((R, NB), cat.start_node, np.int32), beam_width=B, vocab_size=V, csr=cat.csr,
+                hist=np.full((R, NB, 1), cat.sid_begin, np.int32))
+    for r in range(2):
+        assert "error" not in results[r], results[r]
+        assert_step_parity(case, results[r])
+    for k in ("cand_token", "cand_parent", "sel_node", "hist_out"):
+        assert np.array_equal(results[0][k], results[1][k]), k
