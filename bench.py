@@ -17,6 +17,10 @@ so no flush is needed between iterations.
 --gpus N (under torchrun): requests are sharded, every rank runs its own
 batch of the configured size (weak scaling, no collective on the data path);
 the time is the max over ranks of the device-timed region.
+--config cfg5 --gpus N (under torchrun): the vocabulary-sharded step instead:
+every rank holds V/N logit columns of the same requests and the ranks
+exchange per-row partials and per-request top-2B keys by NCCL all-gathers
+(strong scaling: the job is fixed, per-rank bytes shrink with N).
 --impl reference: the CPU restatement of the reference's step (the oracle
 port) on the host cores, on a bounded sample of the same workload.
 """
@@ -47,7 +51,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="cfg2", choices=["cfg2", "cfg3", "cfg4"])
+    ap.add_argument("--config", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -469,10 +473,100 @@ def run_reference(args):
     print(json.dumps(res), flush=True)
 
 
+def run_sharded(args):
+    """Vocabulary-sharded step (cfg5) on N GPUs: each rank V/N columns, NCCL all-gathers."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from vllm_gr_ehaleva_b200.sample.beam_search_sampler import Workspace
+    from vllm_gr_ehaleva_b200.sharded import sharded_beam_step, torch_all_gather
+    from vllm_gr_ehaleva_b200.synthetic import logits_torch
+
+    world = int(os.environ["WORLD_SIZE"])
+    rank = int(os.environ["RANK"])
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    cfg = dict(CONFIGS[args.config])
+    R, B, V = args.requests or cfg["requests"], cfg["beams"], cfg["vocab"]
+    if V % world:
+        raise SystemExit(f"vocab {V} does not split over {world} ranks")
+    VL = V // world
+    cat = make_catalog(cfg["items"], cfg["levels"], cfg["codebook"], V, cfg["zipf"], seed=1)
+    csr = tuple(torch.from_numpy(a).to(device) for a in (cat.csr.row_ptr, cat.csr.child_tok, cat.csr.child_node))
+    levels = cfg["levels"]
+    logits = [logits_torch(R * B, VL, cfg["sigma"], seed=1000 + 17 * lvl + rank, dtype=torch.bfloat16, device=device)
+              for lvl in range(levels)]
+    cum0 = torch.from_numpy(initial_cum(R, B)).to(device)
+    node0 = torch.full((R, B), cat.start_node, dtype=torch.int32, device=device)
+    hist0 = torch.full((R, B, 1), cat.sid_begin, dtype=torch.int32, device=device)
+    ws = Workspace(device)
+    gather = torch_all_gather()
+    stream = torch.cuda.current_stream(device)
+
+    def chain(n):
+        cum, node, hist = cum0, node0, hist0
+        for i in range(n):
+            out = sharded_beam_step(logits[i % levels], cum, node, all_gather=gather, beam_width=B, vocab_size=V,
+                                    vocab_offset=rank * VL, csr=csr, hist=hist, workspace=ws)
+            if (i + 1) % levels == 0:
+                cum, node, hist = cum0, node0, hist0
+            else:
+                cum, node, hist = out.sel_score, out.sel_node, out.hist_out
+        return out
+
+    out = chain(max(args.warmup, 3))
+    torch.cuda.synchronize()
+    err = int(out.err.item())
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    out = chain(args.steps)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    err |= int(out.err.item())
+    t = torch.tensor([t0.elapsed_time(t1)], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    step_ms = ms / args.steps
+    local_bytes = R * B * VL * 2          # this rank's logits, read once per step
+    peak, peak_kind = peaks()
+    achieved = local_bytes / (step_ms * 1e-3) / 1e9
+    res = {
+        "metric": METRIC, "value": round(R * args.steps / (ms * 1e-3), 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(step_ms, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0, sigma^2) logits, Zipf catalog)",
+        "config": {"workload": args.config, "requests": R, "beam_width": B, "vocab": V, "vocab_per_rank": VL,
+                   "parallelism": f"vocab-sharded x{world} (NCCL all-gathers)",
+                   "l2": "per-rank logits larger than L2, no flush"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                     "kernel": "whole sharded step per rank (3 phases + 2 all-gathers)",
+                     "algorithmic_bytes_per_launch": local_bytes},
+        "gpu_launches": 8 * args.steps,
+        "clocks": clk, "device_errors": err,
+    }
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif "shards" in CONFIGS[args.config] and int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        run_sharded(args)
     else:
         run_ours(args)
 

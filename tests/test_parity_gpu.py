@@ -192,3 +192,29 @@ def test_mixed_rows_many_per_cta():
     case = Case(logits32=make_logits(R, NB, V, 4.0, 77, "bf16"), dtype="bf16", cum=initial_cum(R, NB),
                 node=node, beam_width=B, vocab_size=V, csr=cat.csr)
     assert_step_parity(case, gpu_step(case))
+
+
+def test_wide_beam_1024():
+    # B = 1024 (cfg5's beam width): 2B = 2048 candidates per request; a few rows
+    # without a node take the streamed path with its shorter sub-batches
+    cat = small_catalog()
+    R, NB, B, V = 1, 1024, 1024, 8192
+    node = np.full((R, NB), cat.start_node, np.int32)
+    node[0, 7] = -1
+    node[0, 600] = -1
+    case = Case(logits32=make_logits(R, NB, V, 4.0, 91, "bf16"), dtype="bf16", cum=initial_cum(R, NB), node=node,
+                beam_width=B, vocab_size=V, csr=cat.csr)
+    assert_step_parity(case, gpu_step(case))
+
+
+def test_wide_beam_512_three_steps():
+    # cfg3's beam width (2B = 1024: the request score histogram raises the bound)
+    cat = small_catalog()
+    R, NB, B, V = 2, 512, 512, 8192
+    case = Case(logits32=make_logits(R, NB, V, 4.0, 92, "bf16"), dtype="bf16", cum=initial_cum(R, NB),
+                node=np.full((R, NB), cat.start_node, np.int32), beam_width=B, vocab_size=V, csr=cat.csr,
+                hist=np.full((R, NB, 1), cat.sid_begin, np.int32))
+    for step in range(3):
+        gpu = gpu_step(case)
+        assert_step_parity(case, gpu)
+        case = next_inputs(case, gpu, make_logits(R, NB, V, 4.0, 93 + step, "bf16"))

@@ -89,12 +89,14 @@ struct Params {
   // workspace
   unsigned long long* tau;     // [R] running lower bound of the request's 2B-th key
   unsigned int* row_counter;   // next row to hand out (rows taken dynamically by the CTAs)
+  unsigned int* req_hist;      // [R][kReqHistBins] emitted keys per score bin (large 2B only, else null)
   unsigned int* rowcnt;        // [R*NB] keys in each row's slot
   int* meta;                   // [R*NB][kMetaWords] row metadata resolved by row_meta_kernel
   unsigned long long* buf;     // [R*NB][2B] per-row candidate slots
   // derived
   int k2;        // 2B candidates
   int kk;        // streamed keep count: max(2B, K) + slack
+  int sub_vecs;  // streamed rows: 16-byte vectors between key-list capacity checks
   int pen;       // penalty pointers present
   int stages;
   int bm_words;
@@ -116,12 +118,21 @@ struct Params {
 // Row metadata record (kMetaWords 32-bit words), resolved for every row by
 // row_meta_kernel before the fused kernel so that a row's setup is one
 // prefetched load instead of a chain of dependent loads.
+// Request score histogram: bins of 1/16 nat below the request's first beam's
+// cum, kept for steps with 2B >= kReqHistMinK2.  Rows add the keys they emit;
+// the first bin where the count from the top reaches 2B bounds the request's
+// 2B-th key from below (the union of all rows' lists, not one row's).
+constexpr int kReqHistBins = 1024;
+constexpr int kReqHistMinK2 = 512;
+constexpr float kReqHistScale = 16.0f;
+
 constexpr int kMetaSmall = 16;                  // child tokens kept for small nodes
 constexpr int kMetaWords = 32;                  // 128 bytes
 enum MetaWord {
   kMNode = 0, kMCum = 1, kMC0 = 2, kMC1 = 3, kMLo = 4, kMHi = 5,   // node, cum, CSR range, child token bounds
   kMTeff = 6, kMRteff = 7,                                          // effective temperature and its reciprocal
   kMRow = 8, kMR = 9, kMB = 10,                                     // row, request, beam
+  kMRef = 11,                                                       // the request's first beam's cum
   kMToks = 12,                                                      // child tokens of small nodes (16 words)
   kMTauLo = 28, kMTauHi = 29                                        // request threshold (filled on chip)
 };
@@ -907,6 +918,66 @@ struct Step {
     unsigned long long* dst = P.buf + static_cast<size_t>(c.r) * P.NB * static_cast<size_t>(P.k2) + S.v->base;
     const uint64_t keep = l2_policy_evict_last();
     for (int i = threadIdx.x; i < n; i += kThreads) st_keep_u64(dst + i, S.keys[i], keep);
+    if (P.req_hist && n > 0) raise_tau_from_histogram(c, n);
+  }
+
+  // Add this row's emitted keys to its request's score histogram and raise the
+  // request bound to the first bin where the count from the top reaches 2B.
+  __device__ void raise_tau_from_histogram(const RowCtx& c, int n) {
+    const Smem S = smem_view(P);
+    static_assert(kKeyCap / 2 * 2 >= kReqHistBins, "local histogram fits in the key list's upper half");
+    uint32_t* lh = reinterpret_cast<uint32_t*>(S.keys + kKeyCap / 2);   // keys use [0, 2B <= kKeyCap/2)
+    const float ref = __int_as_float(rec[kMRef]);
+    for (int i = threadIdx.x; i < kReqHistBins; i += kThreads) lh[i] = 0u;
+    csync();
+    for (int i = threadIdx.x; i < n; i += kThreads) {
+      const float d = (ref - key_score(S.keys[i])) * kReqHistScale;
+      // above the reference -> bin 0; NaN, -inf and far below -> the catch-all last bin
+      const int bin = (d < 0.0f) ? 0 : ((d >= 0.0f && d < kReqHistBins - 1) ? static_cast<int>(d) : kReqHistBins - 1);
+      atomicAdd(&lh[bin], 1u);
+    }
+    csync();
+    unsigned int* gh = P.req_hist + static_cast<size_t>(c.r) * kReqHistBins;
+    constexpr int kPer = kReqHistBins / kThreads;
+    uint32_t cnt[kPer];
+    uint32_t mine = 0;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      const int bin = threadIdx.x * kPer + q;
+      const uint32_t add = lh[bin];
+      cnt[q] = add ? atomicAdd(gh + bin, add) + add : __ldcg(gh + bin);
+      if (bin == kReqHistBins - 1) cnt[q] = 0;   // the catch-all bin bounds nothing
+      mine += cnt[q];
+    }
+    // exclusive prefix over threads (bins in order: best first)
+    const int lane = lane_id(), warp = warp_id();
+    uint32_t inc = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+      if (lane >= o) inc += v;
+    }
+    float* wsum = S.red_m;   // kWarps words, free outside the row-end normaliser
+    if (lane == 31) wsum[warp] = __uint_as_float(inc);
+    csync();
+    uint32_t before = inc - mine;
+    for (int w = 0; w < warp; ++w) before += __float_as_uint(wsum[w]);
+    if (before < static_cast<uint32_t>(P.k2) && before + mine >= static_cast<uint32_t>(P.k2)) {
+      uint32_t acc = before;
+#pragma unroll
+      for (int q = 0; q < kPer; ++q) {
+        acc += cnt[q];
+        if (acc >= static_cast<uint32_t>(P.k2)) {
+          // 2B emitted keys score at least the lower edge of this bin (one more
+          // bin of margin covers the rounding of the bin arithmetic)
+          const float edge = ref - static_cast<float>(threadIdx.x * kPer + q + 2) / kReqHistScale;
+          const uint64_t cand = static_cast<uint64_t>(f32_to_ord(__fadd_rn(edge, 0.0f))) << 32;
+          atomicMax(P.tau + c.r, static_cast<unsigned long long>(cand));
+          break;
+        }
+      }
+    }
+    csync();
   }
 };
 
@@ -1086,6 +1157,12 @@ __global__ void __launch_bounds__(256) row_meta_kernel(const __grid_constant__ P
   w[kMRow] = row;
   w[kMR] = r;
   w[kMB] = row - r * P.NB;
+  w[kMRef] = __float_as_int(P.cum[static_cast<size_t>(r) * P.NB]);
+  if (P.req_hist) {
+    // this row's share of its request's score histogram, zeroed for the step
+    const int b = row - r * P.NB;
+    for (int i = b; i < kReqHistBins; i += P.NB) P.req_hist[static_cast<size_t>(r) * kReqHistBins + i] = 0u;
+  }
   if (node >= 0) {
     const int c0 = static_cast<int>(P.row_ptr[node]);
     const int c1 = static_cast<int>(P.row_ptr[node + 1]);
@@ -1099,8 +1176,8 @@ __global__ void __launch_bounds__(256) row_meta_kernel(const __grid_constant__ P
     }
   }
   int4* dst = reinterpret_cast<int4*>(P.meta + static_cast<size_t>(row) * kMetaWords);
-#pragma unroll
   const uint64_t keep = l2_policy_evict_last();   // read by the step and merge kernels
+#pragma unroll
   for (int i = 0; i < kMetaWords / 4; ++i) st_keep_v4(dst + i, make_int4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]), keep);
 }
 
@@ -1113,7 +1190,6 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
   constexpr int EPV = Tr::kPerVec;
   constexpr int kChunkElems = kStageBytes / ES;
   constexpr int kChunkVecs = kStageBytes / 16;
-  constexpr int kSubVecs = kBatch / EPV;     // vectors between capacity checks (stream rows)
 
   const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
   const int total = P.R * P.NB;
@@ -1316,8 +1392,8 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
         }
       } else {
         fold(sacc0, sacc1, s);
-        for (int sb = 0; sb < nvec; sb += kSubVecs) {
-          const int send = min(nvec, sb + kSubVecs);
+        for (int sb = 0; sb < nvec; sb += P.sub_vecs) {
+          const int send = min(nvec, sb + P.sub_vecs);
           for (int vb = sb + warp * 32; vb < send; vb += kThreads) {
             const int v = vb + lane;
             const bool valid = v < send;
@@ -1331,7 +1407,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
             st.template process<EPV>(c, x, tbase + v * EPV, valid, m, s, thr_y, thr_key);
           }
           csync();
-          if (static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
+          if (static_cast<int>(S.v->cnt) > kKeyCap - P.sub_vecs * EPV) {
             const Cut cut = st.shrink_to(P.kk);
             if (tid == 0) {
               S.v->discard = 1;
@@ -1580,6 +1656,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
   if (tid == 0) {
     M.cnt[0] = 0;
     M.cnt[1] = 0;
+    M.cnt[2] = 0;
   }
   csync();
   if (tid == 0) {
@@ -1612,7 +1689,10 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
   GR_MPROF();
   // ---- canonical top-2B
   int n = 0;   // keys >= tau gathered into shared memory
-  if (n_all <= kMergeCap) {
+  // the shared-memory path takes every flat list (its keys >= tau almost always
+  // fit) and every slot grid whose keys all fit; an overflow falls back below
+  bool smem_path = (S == 1) || (n_all <= kMergeCap);
+  if (smem_path) {
     // row of every gathered index (one warp per row), then a flat gather with
     // kU independent loads per thread in flight
     if (S > 1) {
@@ -1637,9 +1717,12 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
 #pragma unroll
       for (int u = 0; u < kU; ++u)
         if (base0 + u * kThreads + tid < n_all && kv[u] >= tau && kv[u] != 0ull) mask |= 1u << u;
-      warp_append_n<kU>(mask, kv, M.keys, &M.cnt[0], kMergeCap, &dummy);
+      warp_append_n<kU>(mask, kv, M.keys, &M.cnt[0], kMergeCap, reinterpret_cast<int*>(&M.cnt[2]));
     }
     csync();
+    smem_path = M.cnt[2] == 0;   // no key was dropped
+  }
+  if (smem_path) {
     n = static_cast<int>(M.cnt[0]);
     k = min(k, n);
     GR_MPROF();
@@ -1678,6 +1761,12 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     k = min(k, static_cast<int>(M.cnt[1]));
   }
   GR_MPROF();
+  if (P.keys_out) {
+    // vocab-sharded phase 2: this shard's top-2B keys, unordered (the final
+    // merge sorts), zero padded
+    for (int i = tid; i < k2; i += kThreads) P.keys_out[static_cast<size_t>(r) * k2 + i] = (i < k) ? M.top[i] : 0ull;
+    return;
+  }
   // ---- descending order: rank sort for small k, bitonic otherwise
   if (k <= kThreads) {
     const uint64_t mine = (tid < k) ? M.top[tid] : 0ull;
@@ -1695,62 +1784,98 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     while (P2 < k) P2 <<= 1;
     for (int i = tid; i < P2; i += kThreads) M.keys[i] = (i < k) ? M.top[i] : 0ull;
     csync();
-    cta_bitonic_sort_desc(M.keys, P2);
+    if (P2 == 2 * kThreads) cta_bitonic_sort_regs_desc<2>(M.keys);
+    else if (P2 == 4 * kThreads) cta_bitonic_sort_regs_desc<4>(M.keys);
+    else if (P2 == 8 * kThreads) cta_bitonic_sort_regs_desc<8>(M.keys);
+    else cta_bitonic_sort_desc(M.keys, P2);
   }
   GR_MPROF();
-  if (P.keys_out) {
-    // vocab-sharded phase 2: this shard's canonical top-2B keys, zero padded
-    for (int i = tid; i < k2; i += kThreads) P.keys_out[static_cast<size_t>(r) * k2 + i] = (i < k) ? M.keys[i] : 0ull;
-    return;
-  }
-  // ---- outputs
+  // ---- outputs: kO candidates per thread at a time, every load of a batch
+  // issued before any of them is used
   const int B = P.B, T = P.T;
-  for (int i = tid; i < k2; i += kThreads) {
-    float sc = -kInf;
-    int tok = -1, par = -1, child = GR_NODE_DEAD;
-    if (i < k) {
-      const uint64_t key = M.keys[i];
-      const uint32_t flat = key_flat(key);
-      sc = key_score(key);
-      par = static_cast<int>(flat / static_cast<uint32_t>(P.V));
-      const int x = static_cast<int>(flat - static_cast<uint32_t>(par) * static_cast<uint32_t>(P.V));
-      const int* rec = P.meta + static_cast<size_t>(r * NB + par) * kMetaWords;
-      const int pn = __ldcg(rec + kMNode);
-      if (P.K == 0 && pn >= 0) {
-        // catalog row: the key carries the child's CSR position
-        const int e = __ldcg(rec + kMC0) + x;
-        tok = __ldg(P.child_tok + e);
-        if (i < B) child = __ldg(P.child_node + e);
-      } else {
-        tok = x;
-        if (i < B) child = (pn == GR_NODE_UNCONSTRAINED) ? GR_NODE_UNCONSTRAINED : child_by_search(P, rec, tok);
+  constexpr int kO = 8;
+  for (int i0 = tid; i0 < k2; i0 += kThreads * kO) {
+    int par[kO], x[kO], pn[kO], c0[kO];
+    float sc[kO];
+#pragma unroll
+    for (int u = 0; u < kO; ++u) {
+      const int i = i0 + u * kThreads;
+      sc[u] = -kInf;
+      par[u] = -1;
+      x[u] = 0;
+      if (i < k) {
+        const uint64_t key = M.keys[i];
+        const uint32_t flat = key_flat(key);
+        sc[u] = key_score(key);
+        par[u] = static_cast<int>(flat / static_cast<uint32_t>(P.V));
+        x[u] = static_cast<int>(flat - static_cast<uint32_t>(par[u]) * static_cast<uint32_t>(P.V));
       }
     }
-    if (i < kMergeTop) {
-      M.dec_tok[i] = tok;
-      M.dec_par[i] = par;
+#pragma unroll
+    for (int u = 0; u < kO; ++u) {
+      const int* rec = P.meta + static_cast<size_t>(r * NB + max(par[u], 0)) * kMetaWords;
+      pn[u] = __ldcg(rec + kMNode);
+      c0[u] = __ldcg(rec + kMC0);
     }
-    P.cand_score[static_cast<size_t>(r) * k2 + i] = sc;
-    P.cand_token[static_cast<size_t>(r) * k2 + i] = tok;
-    P.cand_parent[static_cast<size_t>(r) * k2 + i] = par;
-    if (i < B) {
-      P.sel_score[static_cast<size_t>(r) * B + i] = sc;
-      P.sel_token[static_cast<size_t>(r) * B + i] = tok;
-      P.sel_parent[static_cast<size_t>(r) * B + i] = par;
-      P.sel_node[static_cast<size_t>(r) * B + i] = child;
+    int tok[kO], child[kO];
+#pragma unroll
+    for (int u = 0; u < kO; ++u) {
+      const int i = i0 + u * kThreads;
+      tok[u] = -1;
+      child[u] = GR_NODE_DEAD;
+      if (par[u] >= 0 && P.K == 0 && pn[u] >= 0) {
+        // catalog row: the key carries the child's CSR position
+        tok[u] = __ldg(P.child_tok + c0[u] + x[u]);
+        if (i < B) child[u] = __ldg(P.child_node + c0[u] + x[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kO; ++u) {
+      const int i = i0 + u * kThreads;
+      if (i >= k2) continue;
+      if (par[u] >= 0 && !(P.K == 0 && pn[u] >= 0)) {
+        tok[u] = x[u];
+        if (i < B)
+          child[u] = (pn[u] == GR_NODE_UNCONSTRAINED)
+                         ? GR_NODE_UNCONSTRAINED
+                         : child_by_search(P, P.meta + static_cast<size_t>(r * NB + par[u]) * kMetaWords, tok[u]);
+      }
+      if (i < kMergeTop) {
+        M.dec_tok[i] = tok[u];
+        M.dec_par[i] = par[u];
+      }
+      P.cand_score[static_cast<size_t>(r) * k2 + i] = sc[u];
+      P.cand_token[static_cast<size_t>(r) * k2 + i] = tok[u];
+      P.cand_parent[static_cast<size_t>(r) * k2 + i] = par[u];
+      if (i < B) {
+        P.sel_score[static_cast<size_t>(r) * B + i] = sc[u];
+        P.sel_token[static_cast<size_t>(r) * B + i] = tok[u];
+        P.sel_parent[static_cast<size_t>(r) * B + i] = par[u];
+        P.sel_node[static_cast<size_t>(r) * B + i] = child[u];
+      }
     }
   }
   if (P.hist_out) {
     csync();
     const int W = T + 1;
-    for (int idx = tid; idx < B * W; idx += kThreads) {
-      const int i = idx / W, t = idx - i * W;
-      int v = -1;
-      if (i < k) {
-        const int par = M.dec_par[i];
-        v = (t < T) ? P.hist[(static_cast<size_t>(r) * NB + par) * T + t] : M.dec_tok[i];
+    constexpr int kH = 8;   // entries per thread per batch, loads first
+    for (int idx0 = tid; idx0 < B * W; idx0 += kThreads * kH) {
+      int v[kH];
+#pragma unroll
+      for (int u = 0; u < kH; ++u) {
+        const int idx = idx0 + u * kThreads;
+        const int i = idx / W, t = idx - i * W;
+        v[u] = -1;
+        if (idx < B * W && i < k) {
+          const int par = M.dec_par[i];
+          v[u] = (t < T) ? __ldg(P.hist + (static_cast<size_t>(r) * NB + par) * T + t) : M.dec_tok[i];
+        }
       }
-      P.hist_out[static_cast<size_t>(r) * B * W + idx] = v;
+#pragma unroll
+      for (int u = 0; u < kH; ++u) {
+        const int idx = idx0 + u * kThreads;
+        if (idx < B * W) P.hist_out[static_cast<size_t>(r) * B * W + idx] = v[u];
+      }
     }
   }
 #ifdef GR_PHASE_PROFILE
@@ -1825,7 +1950,7 @@ static int validate(const gr_step_desc* d) {
   const int k2 = 2 * d->beam_width;
   if (k2 > kKeyCap / 2) return GR_ERR_UNSUPPORTED;
   const int kk = (k2 > d->per_beam_k ? k2 : d->per_beam_k) + kSlack;
-  if (kk > kKeyCap - kBatch) return GR_ERR_UNSUPPORTED;
+  if (kk + 32 * 8 > kKeyCap) return GR_ERR_UNSUPPORTED;   // room for one warp-wide batch of 2-byte logits
   if (d->num_edges > 0x7FFFFFFFll) return GR_ERR_UNSUPPORTED;
   if (d->num_beams > kMergeMaxBeams) return GR_ERR_UNSUPPORTED;
   return GR_OK;
@@ -1868,6 +1993,13 @@ static void fill_params(Params& P, const gr_step_desc* d, const gr_step_io* io) 
   P.err = io->err;
   P.k2 = 2 * d->beam_width;
   P.kk = (P.k2 > P.K ? P.k2 : P.K) + kSlack;
+  {
+    // streamed rows add at most sub_vecs * EPV keys between shrinks back to kk
+    const int epv = (d->logit_dtype == GR_DTYPE_F32) ? 4 : 8;
+    const int room = (kKeyCap - P.kk < kBatch) ? kKeyCap - P.kk : kBatch;
+    P.sub_vecs = (room / epv) / 32 * 32;
+    if (P.sub_vecs < 32) P.sub_vecs = 32;
+  }
   P.pen = (io->rep_penalty || io->pres_penalty || io->freq_penalty) ? 1 : 0;
   P.bm_words = (d->vocab_local + 31) / 32 + 1;
   P.partial_only = 0;
@@ -2052,6 +2184,8 @@ static int setup_step(const gr_step_desc* d, const gr_step_io* io, void* workspa
   P.meta = reinterpret_cast<int*>(ws + o); o += ws_meta_bytes(R, NB);
   P.buf = reinterpret_cast<unsigned long long*>(ws + o); o += align128(size_t(R) * NB * size_t(P.k2) * 8);
   *lse_ws = reinterpret_cast<float*>(ws + o);
+  o += align128(size_t(R) * NB * 4);
+  P.req_hist = (P.k2 >= kReqHistMinK2) ? reinterpret_cast<unsigned int*>(ws + o) : nullptr;
   const int rows = R * NB;
   row_meta_kernel<<<(rows + 255) / 256, 256, 0, s>>>(P);
   if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
@@ -2106,7 +2240,8 @@ int32_t gr_beam_step_workspace_size(const gr_step_desc* d, size_t* bytes) {
   const size_t slots = size_t(d->num_requests) * d->num_beams * size_t(2 * d->beam_width);
   *bytes = ws_tau_bytes(d->num_requests) + ws_cnt_bytes(d->num_requests, d->num_beams) +
            ws_meta_bytes(d->num_requests, d->num_beams) + align128(slots * 8) +
-           align128(size_t(d->num_requests) * d->num_beams * 4);
+           align128(size_t(d->num_requests) * d->num_beams * 4) +
+           align128(size_t(d->num_requests) * kReqHistBins * 4);
   return GR_OK;
 }
 

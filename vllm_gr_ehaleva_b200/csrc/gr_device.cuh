@@ -423,6 +423,52 @@ __device__ __forceinline__ uint32_t cta_compact(uint64_t* keys, int n, Cut cut, 
   return *cnt;
 }
 
+// Sort a[0..kThreads*E) descending (bitonic).  Thread t holds elements
+// [t*E, t*E + E) in registers: exchange distances below E stay in the thread,
+// below 32E go through warp shuffles, and only the longer ones through shared
+// memory (a[] is the exchange buffer and receives the result).
+template <int E>
+__device__ __forceinline__ void cta_bitonic_sort_regs_desc(uint64_t* a) {
+  constexpr int P = kThreads * E;
+  const int tid = threadIdx.x;
+  uint64_t v[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) v[e] = a[tid * E + e];
+  csync();
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      uint64_t o[E];
+      if (j < E) {
+        // in-thread partners; j is a run-time value, so pick among fixed indices
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[e] = (j == 1) ? v[e ^ 1] : ((j == 2) ? v[(e ^ 2) % E] : v[(e ^ 4) % E]);
+      } else if (j < 32 * E) {
+        const int lanes = j / E;
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[e] = __shfl_xor_sync(0xFFFFFFFFu, v[e], lanes);
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) a[tid * E + e] = v[e];
+        csync();
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[e] = a[(tid * E + e) ^ j];
+        csync();
+      }
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const int i = tid * E + e;
+        const bool lower = (i & j) == 0;          // i < i ^ j
+        const bool desc = (i & k) == 0;           // this run sorts descending
+        const bool take_max = (lower == desc);
+        v[e] = take_max ? (v[e] > o[e] ? v[e] : o[e]) : (v[e] < o[e] ? v[e] : o[e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) a[tid * E + e] = v[e];
+  csync();
+}
+
 // Sort a[0..P) descending; P a power of two.
 __device__ __forceinline__ void cta_bitonic_sort_desc(uint64_t* a, int P) {
   for (int k = 2; k <= P; k <<= 1) {

@@ -404,7 +404,6 @@ __device__ void ws_finish_rows(const Params& P) {
   Step<TL> st(P);
   using Tr = LogitTraits<TL>;
   constexpr int EPV = Tr::kPerVec;
-  constexpr int kSubVecs = kBatch / EPV;
   const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
   for (int it = 0;; ++it) {
     const int slot = it % ws::kSlots;
@@ -508,8 +507,8 @@ __device__ void ws_finish_rows(const Params& P) {
       }
       const uint4* bv = reinterpret_cast<const uint4*>(g.body);
       const int nvec_all = static_cast<int>(g.body_bytes >> 4);
-      for (int sb = 0; sb < nvec_all; sb += kSubVecs) {
-        const int send = min(nvec_all, sb + kSubVecs);
+      for (int sb = 0; sb < nvec_all; sb += P.sub_vecs) {
+        const int send = min(nvec_all, sb + P.sub_vecs);
         for (int vb = sb + warp * 32; vb < send; vb += kThreads) {
           const int v = vb + lane;
           const bool valid = v < send;
@@ -523,7 +522,7 @@ __device__ void ws_finish_rows(const Params& P) {
           st.template process<EPV>(c, x, g.head + v * EPV, valid, dm, ds, thr_y, thr_key);
         }
         csync();
-        if (static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
+        if (static_cast<int>(S.v->cnt) > kKeyCap - P.sub_vecs * EPV) {
           const Cut cut = st.shrink_to(P.kk);
           if (tid == 0) {
             S.v->discard = 1;
