@@ -479,8 +479,7 @@ def run_sharded(args):
 
     import torch
     import torch.distributed as dist
-    from vllm_gr_ehaleva_b200.sample.beam_search_sampler import Workspace
-    from vllm_gr_ehaleva_b200.sharded import sharded_beam_step, torch_all_gather
+    from vllm_gr_ehaleva_b200.sharded import ShardedStepper
     from vllm_gr_ehaleva_b200.synthetic import logits_torch
 
     world = int(os.environ["WORLD_SIZE"])
@@ -502,15 +501,16 @@ def run_sharded(args):
     cum0 = torch.from_numpy(initial_cum(R, B)).to(device)
     node0 = torch.full((R, B), cat.start_node, dtype=torch.int32, device=device)
     hist0 = torch.full((R, B, 1), cat.sid_begin, dtype=torch.int32, device=device)
-    ws = Workspace(device)
-    gather = torch_all_gather()
     stream = torch.cuda.current_stream(device)
+    # one persistent stepper per fork-table length (the table grows by one token per level)
+    steppers = [ShardedStepper(num_requests=R, num_beams=B, beam_width=B, vocab_size=V, vocab_local=VL,
+                               vocab_offset=rank * VL, num_shards=world, csr=csr, hist_len=1 + lvl, device=device)
+                for lvl in range(levels)]
 
     def chain(n):
         cum, node, hist = cum0, node0, hist0
         for i in range(n):
-            out = sharded_beam_step(logits[i % levels], cum, node, all_gather=gather, beam_width=B, vocab_size=V,
-                                    vocab_offset=rank * VL, csr=csr, hist=hist, workspace=ws)
+            out = steppers[i % levels].step(logits[i % levels], cum, node, hist)
             if (i + 1) % levels == 0:
                 cum, node, hist = cum0, node0, hist0
             else:

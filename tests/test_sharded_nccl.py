@@ -45,6 +45,16 @@ def _worker(rank, world, port, q):
         torch.cuda.synchronize()
         res = {k: getattr(out, k).cpu().numpy() for k in OUT_KEYS}
         res["err"] = int(out.err.item())
+        # the persistent stepper gives the same step
+        from vllm_gr_ehaleva_b200.sharded import ShardedStepper
+        stepper = ShardedStepper(num_requests=R, num_beams=NB, beam_width=B, vocab_size=V, vocab_local=VL,
+                                 vocab_offset=rank * VL, num_shards=world, csr=csr, hist_len=1,
+                                 row_stride=local.stride(0), device=dev)
+        out2 = stepper.step(local, torch.from_numpy(case.cum).to(dev), torch.from_numpy(case.node).to(dev),
+                            torch.from_numpy(case.hist).to(dev))
+        torch.cuda.synchronize()
+        res["stepper_same"] = all(np.array_equal(getattr(out2, k).cpu().numpy(), res[k])
+                                  for k in ("cand_score", "cand_token", "cand_parent", "sel_node", "hist_out"))
         q.put((rank, res))
         dist.barrier()
         dist.destroy_process_group()
@@ -75,6 +85,7 @@ def test_sharded_step_two_gpus_nccl():
                 hist=np.full((R, NB, 1), cat.sid_begin, np.int32))
     for r in range(2):
         assert "error" not in results[r], results[r]
+        assert results[r].pop("stepper_same")
         assert_step_parity(case, results[r])
     for k in ("cand_token", "cand_parent", "sel_node", "hist_out"):
         assert np.array_equal(results[0][k], results[1][k]), k

@@ -126,3 +126,86 @@ def torch_all_gather(group=None) -> Callable[[torch.Tensor], torch.Tensor]:
         dist.all_gather(parts, t, group=group)
         return torch.stack(parts)
     return gather
+
+
+class ShardedStepper:
+    """The vocab-sharded step for one batch shape, with its descriptor, device
+    buffers and gather targets built once, so that a step costs three library
+    calls and two all-gathers on the host.  Outputs alternate between two
+    buffer sets: a step's outputs stay valid while the next step runs (they can
+    be its inputs) and are overwritten by the step after that."""
+
+    def __init__(self, *, num_requests: int, num_beams: int, beam_width: int, vocab_size: int, vocab_local: int,
+                 vocab_offset: int, num_shards: int, csr, hist_len: int, logits_dtype=torch.bfloat16,
+                 row_stride: Optional[int] = None, eos_token_id: Optional[int] = None,
+                 all_gather: Optional[Callable[[torch.Tensor], torch.Tensor]] = None, group=None, device=None):
+        from .sample.beam_search_sampler import _DTYPES, make_desc, workspace_size
+        self.lib = _lib.load()
+        self.device = torch.device(device if device is not None else "cuda")
+        R, NB, B, S = int(num_requests), int(num_beams), int(beam_width), int(num_shards)
+        self.R, self.NB, self.B, self.S, self.T = R, NB, B, S, int(hist_len)
+        row_ptr, child_tok, child_node = csr
+        self.csr = csr
+        self.eos = eos_token_id
+        self.desc = make_desc(R=R, NB=NB, B=B, V=int(vocab_size), VL=int(vocab_local), voff=int(vocab_offset),
+                              row_stride=int(row_stride if row_stride is not None else vocab_local),
+                              dtype=_DTYPES[logits_dtype], mode=_lib.LOGPROBS_RAW, K=0,
+                              eos=-1 if eos_token_id is None else int(eos_token_id), T=self.T,
+                              N=int(row_ptr.numel()) - 1, E=int(child_tok.numel()))
+        dev = dict(device=self.device)
+        f32, i32 = dict(dtype=torch.float32, **dev), dict(dtype=torch.int32, **dev)
+        self.outs = [BeamStepOutput(
+            cand_score=torch.empty((R, 2 * B), **f32), cand_token=torch.empty((R, 2 * B), **i32),
+            cand_parent=torch.empty((R, 2 * B), **i32), sel_score=torch.empty((R, B), **f32),
+            sel_token=torch.empty((R, B), **i32), sel_parent=torch.empty((R, B), **i32),
+            sel_node=torch.empty((R, B), **i32), eos_score=torch.empty((R, NB), **f32),
+            hist_out=torch.empty((R, B, self.T + 1), **i32), lse=torch.empty((R, NB), **f32),
+            err=torch.zeros(1, **i32)) for _ in range(2)]
+        self.partials = torch.empty((R * NB, 2), **f32)
+        self.keys = torch.empty((R, 2 * B), dtype=torch.int64, **dev)
+        self.gathered_p = torch.empty((S, R * NB, 2), **f32)
+        self.gathered_k = torch.empty((S, R, 2 * B), dtype=torch.int64, **dev)
+        self.eos_all = torch.empty((S, R, NB), **f32)
+        self.ws = torch.empty(max(workspace_size(self.desc), 256), dtype=torch.uint8, **dev)
+        self.group = group
+        self.gather_fn = all_gather
+        self.k = 0
+
+    def _gather(self, dst: torch.Tensor, src: torch.Tensor) -> None:
+        if self.gather_fn is not None:
+            dst.copy_(self.gather_fn(src))
+            return
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(dst, src, group=self.group)
+
+    def step(self, local_logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor,
+             hist: Optional[torch.Tensor] = None) -> BeamStepOutput:
+        out = self.outs[self.k & 1]
+        self.k += 1
+        io = _lib.StepIO()
+        row_ptr, child_tok, child_node = self.csr
+        vp = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        io.logits, io.cum, io.node, io.hist_in = vp(local_logits), vp(cum), vp(node), vp(hist)
+        io.row_ptr, io.child_tok, io.child_node = vp(row_ptr), vp(child_tok), vp(child_node)
+        io.cand_score, io.cand_token, io.cand_parent = vp(out.cand_score), vp(out.cand_token), vp(out.cand_parent)
+        io.sel_score, io.sel_token, io.sel_parent, io.sel_node = (vp(out.sel_score), vp(out.sel_token),
+                                                                   vp(out.sel_parent), vp(out.sel_node))
+        io.eos_score, io.hist_out, io.lse, io.err = vp(out.eos_score), vp(out.hist_out), vp(out.lse), vp(out.err)
+        out.err.zero_()
+        s = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        d, iop = ctypes.byref(self.desc), ctypes.byref(io)
+        wsp, wsn = ctypes.c_void_p(self.ws.data_ptr()), ctypes.c_size_t(self.ws.numel())
+        _lib.check(self.lib.gr_lse_partials(d, iop, vp(self.partials), wsp, wsn, s), "gr_lse_partials")
+        self._gather(self.gathered_p, self.partials)
+        _lib.check(self.lib.gr_shard_candidates(d, iop, vp(self.gathered_p), ctypes.c_int32(self.S), vp(self.keys),
+                                                wsp, wsn, s), "gr_shard_candidates")
+        self._gather(self.gathered_k, self.keys)
+        _lib.check(self.lib.gr_merge_candidates(d, iop, vp(self.gathered_k), ctypes.c_int32(self.S), wsp, wsn, s),
+                   "gr_merge_candidates")
+        if self.eos is not None:
+            self._gather(self.eos_all, out.eos_score)
+            eos = self.eos_all[0]
+            for k in range(1, self.S):
+                eos = torch.where(torch.isnan(eos), self.eos_all[k], eos)
+            out.eos_score.copy_(eos)
+        return out
