@@ -33,13 +33,19 @@ constexpr int kStrWarps = GR_WS_STREAM_WARPS;
 constexpr int kStrThreads = kStrWarps * 32;
 constexpr int kProdWarp = kFinWarps + kStrWarps;
 constexpr int kBlockWs = (kProdWarp + 1) * 32;
-constexpr int kVecPerThread = 4;
+#ifndef GR_WS_VPT
+#define GR_WS_VPT 4
+#endif
+constexpr int kVecPerThread = GR_WS_VPT;
 constexpr int kStage = kStrThreads * kVecPerThread * 16;   // 4 vectors per streaming thread per stage
 constexpr int kMaxStagesWs = kMaxStages;          // full/empty barriers live in the common layout
 
 // Rows rotate through kSlots slots (record, child window, partials), so the
 // producer can run two rows ahead of the row-end warps.
-constexpr int kSlots = 3;
+#ifndef GR_WS_SLOTS
+#define GR_WS_SLOTS 3
+#endif
+constexpr int kSlots = GR_WS_SLOTS;
 
 // Pieces after the common fixed layout (the penalty pieces are never used here).
 constexpr size_t kOffWin1 = kOffVar;                                      // slots 1.. child windows
