@@ -218,3 +218,24 @@ def test_wide_beam_512_three_steps():
         gpu = gpu_step(case)
         assert_step_parity(case, gpu)
         case = next_inputs(case, gpu, make_logits(R, NB, V, 4.0, 93 + step, "bf16"))
+
+
+@pytest.mark.parametrize("dtype,mode", [("f32", "processed_logprobs"), ("bf16", "raw_logprobs")])
+def test_unconstrained_full_vocab_many_rows(dtype, mode):
+    # cfg4's geometry (V=152064, 64 penalised history tokens per beam) on 2
+    # requests of 48 beams: later rows of a request filter their stream against
+    # the request bound published by earlier rows; two steps
+    R, NB, B, V, H = 2, 48, 48, 152064, 64
+    sigma = 3.0
+    kw = {}
+    if mode == "processed_logprobs":
+        kw = dict(temperature=[0.7, 0.7], rep=[1.2, 1.2], pres=[0.5, 0.5], freq=[0.0, 0.0])
+    case = Case(logits32=make_logits(R, NB, V, sigma, 31, dtype), dtype=dtype, cum=initial_cum(R, NB),
+                node=np.full((R, NB), -1, np.int32), beam_width=B, vocab_size=V,
+                hist=histories(R, NB, H, V, seed=5), mode=mode, **kw)
+    for step in range(2):
+        gpu = gpu_step(case)
+        assert_step_parity(case, gpu)
+        nxt = next_inputs(case, gpu, make_logits(R, NB, V, sigma, 60 + step, dtype))
+        nxt.hist = case.hist     # fixed-length penalty history, as in the benchmark
+        case = nxt

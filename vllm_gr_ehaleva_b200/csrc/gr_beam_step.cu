@@ -155,6 +155,7 @@ struct Scalars {
   uint64_t thr_key;
   uint64_t min_key;
   uint64_t tau_pref;
+  float lse_w[kWarps];         // streamed rows: each warp's log-sum-exp so far (cta_floor)
   long long issued;
   int producer_done;
 #ifdef GR_PHASE_PROFILE
@@ -381,9 +382,12 @@ struct Step {
 
   // Process N consecutive columns starting at local column tb (x = raw values,
   // valid = lane holds real data).  Warp-uniform call.
+  // y_floor: streamed rows skip elements below it (-inf: none); see cta_floor().
+  // lse = false: (m, s) already hold these columns; only the candidate part runs.
   template <int N>
   __device__ __forceinline__ void process(const RowCtx& c, const float* x, int tb, bool valid, float& m, float& s,
-                                          float thr_y, uint64_t thr_key) const {
+                                          float thr_y, uint64_t thr_key, float y_floor = -__builtin_huge_valf(),
+                                          bool lse = true) const {
     const Smem S = smem_view(P);
     float y[N];
 #pragma unroll
@@ -400,7 +404,7 @@ struct Step {
           if ((fl >> i) & 1u) y[i] = -kInf;
       }
     }
-    if (valid) {
+    if (valid && lse) {
       lse_update<N>(y, m, s);
       if (c.constrained && tb + N > c.wlo && tb <= c.whi) {
 #pragma unroll
@@ -411,25 +415,60 @@ struct Step {
       }
     }
     if (c.stream) {
+      const float thr_e = fmaxf(thr_y, y_floor);
       bool any = false;
 #pragma unroll
-      for (int i = 0; i < N; ++i) any |= valid && !((fl >> i) & 1u) && (y[i] >= thr_y);
+      for (int i = 0; i < N; ++i) any |= valid && !((fl >> i) & 1u) && (y[i] >= thr_e);
       if (__any_sync(0xFFFFFFFFu, any)) {
         const uint32_t fbase = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V) +
                                static_cast<uint32_t>(P.voff + tb);
+        uint64_t kv[N];
+        uint32_t mask = 0;
 #pragma unroll
         for (int i = 0; i < N; ++i) {
-          bool pred = valid && !((fl >> i) & 1u) && (y[i] >= thr_y);
-          uint64_t key = 0;
-          if (pred) {
+          kv[i] = 0;
+          if (valid && !((fl >> i) & 1u) && (y[i] >= thr_e)) {
             const float ye = (P.mode == kModeProcessed && c.teff != 1.0f) ? __fdiv_rn(x[i], c.teff) : x[i];
-            key = make_key(ye, fbase + i);
-            pred = key >= thr_key;
+            kv[i] = make_key(ye, fbase + i);
+            if (kv[i] >= thr_key) mask |= 1u << i;
           }
-          warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
         }
+        warp_append_n<N>(mask, kv, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);   // one reservation per warp
       }
     }
+  }
+
+  // Lowest y a streamed element needs to reach the request bound tau: its score
+  // cum + y - lse must be >= tau's score, and lse is at least the log-sum-exp of
+  // the columns seen so far.  Each warp publishes the log-sum-exp of the columns
+  // it has seen in lse_w (one float, reset to -inf at the row start); the other
+  // warps' values are at most one stage old and so still lower bounds of their
+  // final sums.  (m, s) are the calling thread's running max and sum.
+  // Warp-collective; -inf when there is no bound yet.
+  __device__ __forceinline__ float cta_floor(const RowCtx& c, uint64_t tau, float m, float s, float* lse_w) const {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float M = m;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+    float t = (m == -kInf) ? 0.0f : s * fast_exp2((m - M) * kLog2e);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xFFFFFFFFu, t, o);
+    const float Lw = (M > -kInf && t > 0.0f && t < kInf) ? M + logf(t) : -kInf;
+    float Lo[kWarps];
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) Lo[w] = (w == warp) ? Lw : lse_w[w];
+    if (lane == 0) lse_w[warp] = Lw;
+    if (tau == 0ull) return -kInf;
+    float Lm = -kInf;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) Lm = fmaxf(Lm, Lo[w]);
+    if (!(Lm > -kInf && Lm < kInf)) return -kInf;
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) tot += fast_exp2((Lo[w] - Lm) * kLog2e);
+    const float f = key_score(tau) - c.cum + (Lm + logf(tot));
+    if (!(f > -kInf && f < kInf)) return -kInf;
+    return f - fabsf(f) * 1.0e-5f - 1e-30f;   // margin for y vs the exact quotient and the roundings
   }
 
   // ---- selection helpers ------------------------------------------------------
@@ -781,7 +820,10 @@ struct Step {
       P.eos_score[c.row] = __fadd_rn(c.cum, __fsub_rn(y, lse));
     }
     csync();
-    if (n > P.k2) shrink_to(P.k2);
+    if (n > P.k2) {
+      const Cut cut = shrink_to(P.k2);
+      if (P.K == 0) raise_tau(c.r, cut.floor_key());   // the row's 2B-th key bounds the request
+    }
     if (discarded && n > 0) {
       const float s_last = __fadd_rn(c.cum, __fsub_rn(y_last, lse));
       const float s_kth = key_score(min_key_of_list());
@@ -1249,6 +1291,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
       S.v->thr_y = -kInf;
       if (P.eos_score && !P.partial_only) P.eos_score[c.row] = __int_as_float(0x7FC00000);
     }
+    if (tid < kWarps) S.v->lse_w[tid] = -kInf;
     csync();
     if (c.pen_active) {
       const int* h = P.hist + static_cast<size_t>(c.row) * P.T;
@@ -1279,6 +1322,9 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
     float m = -kInf, s = 0.0f;
     float thr_y = -kInf;
     uint64_t thr_key = 0ull;
+    // streamed top-2B rows: the request bound as read one chunk earlier
+    const bool bounded = c.stream && P.K == 0 && !P.partial_only;
+    uint64_t tau_seen = bounded ? *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r) : 0ull;
     const Geom g = row_geom<ES>(P, c.row);
     // whole-vector window copies need vectors that start on window-vector boundaries
     const bool win_vec_ok = (g.head % EPV) == 0;
@@ -1299,6 +1345,27 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
         st.template process<1>(c, x, tl, valid, m, s, thr_y, thr_key);
       }
     }
+    // list length after the last complete append round (bounded rows)
+    uint32_t cnt_prev = 0;
+    if (bounded) {
+      csync();
+      cnt_prev = S.v->cnt;
+    }
+    // shrink the row's list back to its best kk keys; the kk-th bounds the rest of the row
+    auto shrink_row = [&]() {
+      const Cut cut = st.shrink_to(P.kk);
+      if (tid == 0) {
+        S.v->discard = 1;
+        S.v->thr_key = cut.floor_key();
+        const float ty = key_score(cut.floor_key());
+        S.v->thr_y = ty - fabsf(ty) * 2.0e-6f - 1e-30f;
+      }
+      csync();
+      thr_key = S.v->thr_key;
+      thr_y = S.v->thr_y;
+    };
+    const uint32_t shrink_at = max(static_cast<uint32_t>(kKeyCap - 1024),
+                                   static_cast<uint32_t>(P.kk + (kKeyCap - P.kk) / 2));
 
     // ------------------------------------------------------------ body chunks
     GR_PROF_ADD(5, t_row);
@@ -1376,6 +1443,151 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
             }
           }
         }
+      } else if (bounded) {
+        // streamed top-2B row: the exponential sum of the whole stage first, then
+        // a candidate pass against the request bound through a lower bound of the
+        // row's lse; survivors get list slots with one reservation per warp and
+        // one CTA barrier per stage
+        constexpr int kVecPerThread = kChunkVecs / kThreads;
+        const float y_scale = (P.mode == kModeProcessed) ? c.rteff : 1.0f;
+        const uint64_t tau_use = tau_seen;
+        tau_seen = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
+        uint4 vv[kVecPerThread];
+        uint32_t flv[kVecPerThread];
+#pragma unroll
+        for (int j = 0; j < kVecPerThread; ++j) {
+          const int v = tid + j * kThreads;
+          vv[j] = (v < nvec) ? sv[v] : make_uint4(0, 0, 0, 0);
+          flv[j] = 0;
+          if (c.excl && v < nvec) {
+            // penalised columns take their exact values at the row end
+            const int tb = tbase + v * EPV;
+            const int w = tb >> 5, sh = tb & 31;
+            uint64_t bits = S.bitmap[w];
+            if (w + 1 < P.bm_words) bits |= static_cast<uint64_t>(S.bitmap[w + 1]) << 32;
+            flv[j] = static_cast<uint32_t>(bits >> sh) & ((1u << EPV) - 1u);
+            if (flv[j]) Tr::mask_neg_inf(vv[j], flv[j]);
+          }
+        }
+        if (m == -kInf) {
+          float mx = -kInf;
+#pragma unroll
+          for (int j = 0; j < kVecPerThread; ++j) {
+            if (tid + j * kThreads < nvec) {
+              float x[EPV];
+              Tr::unpack(vv[j], x);
+#pragma unroll
+              for (int i = 0; i < EPV; ++i) mx = fmaxf(mx, x[i]);
+            }
+          }
+          m = (P.mode == kModeProcessed) ? mx * c.rteff : mx;
+        }
+        {
+          const float cm = -m * kLog2e;
+          const uint64_t A2 = pack2(a, a), C2 = pack2(cm, cm);
+          uint64_t p0 = pack2(0.0f, 0.0f), p1 = pack2(0.0f, 0.0f);
+#pragma unroll
+          for (int j = 0; j < kVecPerThread; ++j)
+            if (tid + j * kThreads < nvec) FastSum<TL>::add(vv[j], A2, C2, p0, p1);
+          float q0, q1, q2, q3;
+          unpack2(p0, q0, q1);
+          unpack2(p1, q2, q3);
+          const float tot = (q0 + q1) + (q2 + q3);
+          if (tot <= 1.0e30f) {
+            s += tot;
+          } else {
+#pragma unroll
+            for (int j = 0; j < kVecPerThread; ++j) {
+              if (tid + j * kThreads < nvec) {
+                float x[EPV];
+                Tr::unpack(vv[j], x);
+                float y[EPV];
+#pragma unroll
+                for (int i = 0; i < EPV; ++i) y[i] = (P.mode == kModeProcessed) ? x[i] * c.rteff : x[i];
+                st.template lse_update<EPV>(y, m, s);
+              }
+            }
+          }
+        }
+        const float floor_y = st.cta_floor(c, tau_use, m, s, S.v->lse_w);
+        const float thr_e = fmaxf(thr_y, floor_y);
+        // survivors: bit j * EPV + i for element i of vector j
+        uint32_t pm = 0;
+#pragma unroll
+        for (int j = 0; j < kVecPerThread; ++j) {
+          if (tid + j * kThreads < nvec) {
+            float x[EPV];
+            Tr::unpack(vv[j], x);
+            float vmax = x[0];
+#pragma unroll
+            for (int i = 1; i < EPV; ++i) vmax = fmaxf(vmax, x[i]);
+            if (vmax * y_scale >= thr_e) {
+#pragma unroll
+              for (int i = 0; i < EPV; ++i)
+                if (!((flv[j] >> i) & 1u) && x[i] * y_scale >= thr_e) pm |= 1u << (j * EPV + i);
+            }
+          }
+        }
+        const uint32_t cl = static_cast<uint32_t>(__popc(pm));
+        uint32_t inc = cl;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+          if (lane >= o) inc += t;
+        }
+        const uint32_t wtot = __shfl_sync(0xFFFFFFFFu, inc, 31);
+        uint32_t base = 0;
+        if (lane == 31 && wtot) base = atomicAdd(&S.v->cnt, wtot);
+        base = __shfl_sync(0xFFFFFFFFu, base, 31);
+        csync();
+        const uint32_t cnt_now = S.v->cnt;
+        if (cnt_now <= static_cast<uint32_t>(kKeyCap)) {
+          if (cl) {
+            const unsigned char* stage_p = S.ring + static_cast<size_t>(cstage) * kStageBytes;
+            const uint32_t fbase = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V) +
+                                   static_cast<uint32_t>(P.voff + tbase);
+            uint32_t pos = base + inc - cl;
+            uint32_t mk = pm;
+            while (mk) {
+              const int e = __ffs(mk) - 1;
+              mk &= mk - 1u;
+              const int col = (tid + (e / EPV) * kThreads) * EPV + (e % EPV);
+              const float x = Tr::load_s(stage_p, col);
+              const float ye = (P.mode == kModeProcessed && c.teff != 1.0f) ? __fdiv_rn(x, c.teff) : x;
+              S.keys[pos++] = make_key(ye, fbase + static_cast<uint32_t>(col));
+            }
+          }
+          cnt_prev = cnt_now;
+        } else {
+          // the reservations do not fit: undo them and append this stage in
+          // sub-batches with capacity checks (the sums are already in m, s)
+          csync();
+          if (tid == 0) S.v->cnt = cnt_prev;
+          csync();
+          for (int sb = 0; sb < nvec; sb += P.sub_vecs) {
+            const int send = min(nvec, sb + P.sub_vecs);
+            for (int vb = sb + warp * 32; vb < send; vb += kThreads) {
+              const int v = vb + lane;
+              const bool valid = v < send;
+              float x[EPV];
+              if (valid) {
+                Tr::unpack(sv[v], x);
+              } else {
+#pragma unroll
+                for (int i = 0; i < EPV; ++i) x[i] = -kInf;
+              }
+              st.template process<EPV>(c, x, tbase + v * EPV, valid, m, s, thr_y, thr_key, floor_y, false);
+            }
+            csync();
+            if (static_cast<int>(S.v->cnt) > kKeyCap - P.sub_vecs * EPV) shrink_row();
+          }
+          cnt_prev = S.v->cnt;
+        }
+        if (cnt_prev > shrink_at) {
+          csync();
+          shrink_row();
+          cnt_prev = S.v->cnt;
+        }
       } else if (!c.stream) {
         fold(sacc0, sacc1, s);
         for (int vb = warp * 32; vb < nvec; vb += kThreads) {
@@ -1391,6 +1603,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
           st.template process<EPV>(c, x, tbase + v * EPV, valid, m, s, thr_y, thr_key);
         }
       } else {
+        // per-beam top-K rows (and vocab-sharded partial rows) keep every element
         fold(sacc0, sacc1, s);
         for (int sb = 0; sb < nvec; sb += P.sub_vecs) {
           const int send = min(nvec, sb + P.sub_vecs);
@@ -1407,18 +1620,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
             st.template process<EPV>(c, x, tbase + v * EPV, valid, m, s, thr_y, thr_key);
           }
           csync();
-          if (static_cast<int>(S.v->cnt) > kKeyCap - P.sub_vecs * EPV) {
-            const Cut cut = st.shrink_to(P.kk);
-            if (tid == 0) {
-              S.v->discard = 1;
-              S.v->thr_key = cut.floor_key();
-              const float ty = key_score(cut.floor_key());
-              S.v->thr_y = ty - fabsf(ty) * 2.0e-6f - 1e-30f;
-            }
-            csync();
-            thr_key = S.v->thr_key;
-            thr_y = S.v->thr_y;
-          }
+          if (static_cast<int>(S.v->cnt) > kKeyCap - P.sub_vecs * EPV) shrink_row();
         }
       }
       __syncwarp();

@@ -498,7 +498,29 @@ template <> struct LogitTraits<float> {
     x[2] = __uint_as_float(v.z); x[3] = __uint_as_float(v.w);
   }
   __device__ static __forceinline__ float load1(const float* p) { return __ldg(p); }
+  // element i of a shared-memory copy
+  __device__ static __forceinline__ float load_s(const unsigned char* base, int i) {
+    return reinterpret_cast<const float*>(base)[i];
+  }
+  // set the elements whose bit is set in fl (bit i = element i) to -inf
+  __device__ static __forceinline__ void mask_neg_inf(uint4& v, uint32_t fl) {
+    if (fl & 1u) v.x = 0xFF800000u;
+    if (fl & 2u) v.y = 0xFF800000u;
+    if (fl & 4u) v.z = 0xFF800000u;
+    if (fl & 8u) v.w = 0xFF800000u;
+  }
 };
+
+// 2-byte logits: element 2k is the low half of word k, element 2k+1 the high half
+__device__ __forceinline__ void mask_neg_inf_u16(uint4& v, uint32_t fl, uint32_t ninf) {
+  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if ((fl >> (2 * k)) & 1u) w[k] = (w[k] & 0xFFFF0000u) | ninf;
+    if ((fl >> (2 * k + 1)) & 1u) w[k] = (w[k] & 0x0000FFFFu) | (ninf << 16);
+  }
+  v = make_uint4(w[0], w[1], w[2], w[3]);
+}
 template <> struct LogitTraits<__nv_bfloat16> {
   static constexpr int kPerVec = 8;
   __device__ static __forceinline__ void unpack(const uint4& v, float* x) {
@@ -513,6 +535,10 @@ template <> struct LogitTraits<__nv_bfloat16> {
     const unsigned short u = __ldg(reinterpret_cast<const unsigned short*>(p));
     return __uint_as_float(static_cast<uint32_t>(u) << 16);
   }
+  __device__ static __forceinline__ float load_s(const unsigned char* base, int i) {
+    return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const unsigned short*>(base)[i]) << 16);
+  }
+  __device__ static __forceinline__ void mask_neg_inf(uint4& v, uint32_t fl) { mask_neg_inf_u16(v, fl, 0xFF80u); }
 };
 template <> struct LogitTraits<__half> {
   static constexpr int kPerVec = 8;
@@ -527,6 +553,10 @@ template <> struct LogitTraits<__half> {
     }
   }
   __device__ static __forceinline__ float load1(const __half* p) { return __half2float(__ldg(p)); }
+  __device__ static __forceinline__ float load_s(const unsigned char* base, int i) {
+    return __half2float(reinterpret_cast<const __half*>(base)[i]);
+  }
+  __device__ static __forceinline__ void mask_neg_inf(uint4& v, uint32_t fl) { mask_neg_inf_u16(v, fl, 0xFC00u); }
 };
 
 }  // namespace gr

@@ -513,8 +513,17 @@ __device__ void ws_finish_rows(const Params& P) {
       }
       const uint4* bv = reinterpret_cast<const uint4*>(g.body);
       const int nvec_all = static_cast<int>(g.body_bytes >> 4);
+      uint64_t tau_seen = 0ull;
       for (int sb = 0; sb < nvec_all; sb += P.sub_vecs) {
         const int send = min(nvec_all, sb + P.sub_vecs);
+        // the request bound as read one sub-batch earlier; this pass knows the
+        // row's lse exactly, so the bound needs no estimate of it
+        float tau_off = -kInf;
+        if (tau_seen) {
+          const float f = key_score(tau_seen) - c.cum + lse;
+          tau_off = f - fabsf(f) * 1.0e-5f - 1e-30f;   // margin for the roundings of the exact score
+        }
+        tau_seen = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
         for (int vb = sb + warp * 32; vb < send; vb += kThreads) {
           const int v = vb + lane;
           const bool valid = v < send;
@@ -525,7 +534,7 @@ __device__ void ws_finish_rows(const Params& P) {
 #pragma unroll
             for (int i = 0; i < EPV; ++i) x[i] = -kInf;
           }
-          st.template process<EPV>(c, x, g.head + v * EPV, valid, dm, ds, thr_y, thr_key);
+          st.template process<EPV>(c, x, g.head + v * EPV, valid, dm, ds, thr_y, thr_key, tau_off);
         }
         csync();
         if (static_cast<int>(S.v->cnt) > kKeyCap - P.sub_vecs * EPV) {
