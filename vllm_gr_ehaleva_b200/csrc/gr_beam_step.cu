@@ -45,6 +45,8 @@ __device__ unsigned long long g_phase[1024][kProfSlots];
   do { if (threadIdx.x == 0) S.v->prof[slot] += clock64() - (t0); } while (0)
 #define GR_PROF_CNT(slot) \
   do { if (threadIdx.x == 0) S.v->prof[slot] += 1; } while (0)
+#define GR_PROF_VAL(slot, val) \
+  do { if (threadIdx.x == 0) S.v->prof[slot] += (val); } while (0)
 #define GR_PROF_INIT() \
   do { if (threadIdx.x < kProfSlots) S.v->prof[threadIdx.x] = 0; } while (0)
 #define GR_PROF_FLUSH() \
@@ -53,6 +55,7 @@ __device__ unsigned long long g_phase[1024][kProfSlots];
 #define GR_PROF_T(var)
 #define GR_PROF_ADD(slot, t0) do { } while (0)
 #define GR_PROF_CNT(slot) do { } while (0)
+#define GR_PROF_VAL(slot, val) do { } while (0)
 #define GR_PROF_INIT() do { } while (0)
 #define GR_PROF_FLUSH() do { } while (0)
 #endif
@@ -100,6 +103,8 @@ struct Params {
   int pen;       // penalty pointers present
   int stages;
   int bm_words;
+  int tab_cap;   // penalty table entries (>= the history length)
+  int win_bytes; // child window bytes (0: no constrained rows in the step)
   int partial_only;   // 1: write (max, sumexp) partials only (vocab-sharded phase 1)
   float2* partials;
   const float* lse_in;            // vocab-sharded phase 2: the rows' global normaliser (no streaming)
@@ -166,19 +171,21 @@ struct Scalars {
 __host__ __device__ constexpr size_t align128(size_t x) { return (x + 127) & ~size_t(127); }
 
 constexpr size_t kOffKeys = 0;
-constexpr size_t kOffWin = kOffKeys + align128(size_t(kKeyCap) * 8);
-constexpr size_t kOffSel = kOffWin + align128(size_t(kWinBytes));
+constexpr size_t kOffSel = kOffKeys + align128(size_t(kKeyCap) * 8);
 constexpr size_t kOffRed = kOffSel + align128(sizeof(SelectScratch));
 constexpr size_t kOffBars = kOffRed + align128(kWarps * 8);
 constexpr size_t kOffScal = kOffBars + align128(kMaxStages * 16);
-constexpr size_t kOffVar = kOffScal + align128(sizeof(Scalars));
+// the per-step pieces follow: the child window (steps with a catalog), the
+// penalty bitmap and table (steps with penalties), the ring
+constexpr size_t kOffWin = kOffScal + align128(sizeof(Scalars));
 
-__host__ __device__ inline size_t pen_bytes(int bm_words, int pen) {
-  return pen ? align128(size_t(bm_words) * 4) + align128(size_t(kPenTableMax) * 12) : 0;
+__host__ __device__ inline size_t pen_bytes(int bm_words, int tab_cap, int pen) {
+  return pen ? align128(size_t(bm_words) * 4) + align128(size_t(tab_cap) * 12) : 0;
 }
 
-__host__ __device__ inline size_t smem_bytes(int stages, int bm_words, int pen) {
-  return kOffVar + pen_bytes(bm_words, pen) + align128(size_t(stages) * kStageBytes);
+__host__ __device__ inline size_t smem_bytes(int stages, int win_bytes, int bm_words, int tab_cap, int pen) {
+  return kOffWin + align128(size_t(win_bytes)) + pen_bytes(bm_words, tab_cap, pen) +
+         align128(size_t(stages) * kStageBytes);
 }
 
 extern __shared__ __align__(128) unsigned char g_smem[];
@@ -210,12 +217,13 @@ __device__ __forceinline__ Smem smem_view(const Params& P) {
   S.full = reinterpret_cast<uint64_t*>(g_smem + kOffBars);
   S.empty = S.full + kMaxStages;
   S.v = reinterpret_cast<Scalars*>(g_smem + kOffScal);
-  S.bitmap = reinterpret_cast<uint32_t*>(g_smem + kOffVar);
-  const size_t tab = kOffVar + align128(size_t(P.bm_words) * 4);
+  const size_t var = kOffWin + align128(size_t(P.win_bytes));
+  S.bitmap = reinterpret_cast<uint32_t*>(g_smem + var);
+  const size_t tab = var + align128(size_t(P.bm_words) * 4);
   S.tab_tok = reinterpret_cast<int*>(g_smem + tab);
-  S.tab_xp = reinterpret_cast<float*>(g_smem + tab + kPenTableMax * 4);
-  S.tab_y = reinterpret_cast<float*>(g_smem + tab + kPenTableMax * 8);
-  S.ring = g_smem + kOffVar + pen_bytes(P.bm_words, P.pen);
+  S.tab_xp = reinterpret_cast<float*>(g_smem + tab + size_t(P.tab_cap) * 4);
+  S.tab_y = reinterpret_cast<float*>(g_smem + tab + size_t(P.tab_cap) * 8);
+  S.ring = g_smem + var + pen_bytes(P.bm_words, P.tab_cap, P.pen);
   return S;
 }
 
@@ -1541,6 +1549,9 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
         base = __shfl_sync(0xFFFFFFFFu, base, 31);
         csync();
         const uint32_t cnt_now = S.v->cnt;
+        GR_PROF_VAL(12, cnt_now - cnt_prev);
+        GR_PROF_VAL(14, floor_y > -kInf ? 1 : 0);
+        GR_PROF_CNT(15);
         if (cnt_now <= static_cast<uint32_t>(kKeyCap)) {
           if (cl) {
             const unsigned char* stage_p = S.ring + static_cast<size_t>(cstage) * kStageBytes;
@@ -1561,6 +1572,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
         } else {
           // the reservations do not fit: undo them and append this stage in
           // sub-batches with capacity checks (the sums are already in m, s)
+          GR_PROF_CNT(13);
           csync();
           if (tid == 0) S.v->cnt = cnt_prev;
           csync();
@@ -2204,6 +2216,8 @@ static void fill_params(Params& P, const gr_step_desc* d, const gr_step_io* io) 
   }
   P.pen = (io->rep_penalty || io->pres_penalty || io->freq_penalty) ? 1 : 0;
   P.bm_words = (d->vocab_local + 31) / 32 + 1;
+  P.tab_cap = P.pen ? ((d->hist_len > 0 ? d->hist_len : 1) + 31) / 32 * 32 : 0;
+  P.win_bytes = (d->num_nodes > 0 && P.K == 0) ? kWinBytes : 0;
   P.partial_only = 0;
   P.partials = nullptr;
   P.lse_in = nullptr;
@@ -2222,14 +2236,14 @@ static int pick_stages(const Params& P, const DeviceInfo* dev, int* ctas_per_sm)
   const size_t per_sm = static_cast<size_t>(dev->smem_per_sm);
   const size_t rsv = static_cast<size_t>(dev->smem_reserved);
   for (int st = kMaxStages; st >= 3; --st) {
-    const size_t b = smem_bytes(st, P.bm_words, P.pen);
+    const size_t b = smem_bytes(st, P.win_bytes, P.bm_words, P.tab_cap, P.pen);
     if (b <= optin && 2 * (b + rsv) <= per_sm) {
       *ctas_per_sm = 2;
       return st;
     }
   }
   for (int st = kMaxStages; st >= 2; --st) {
-    if (smem_bytes(st, P.bm_words, P.pen) <= optin) {
+    if (smem_bytes(st, P.win_bytes, P.bm_words, P.tab_cap, P.pen) <= optin) {
       *ctas_per_sm = 1;
       return st;
     }
@@ -2243,7 +2257,7 @@ static int launch_fused(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream_t 
   const int stages = pick_stages(P, dev, &per);
   if (stages == 0) return GR_ERR_UNSUPPORTED;
   P.stages = stages;
-  const size_t smem = smem_bytes(stages, P.bm_words, P.pen);
+  const size_t smem = smem_bytes(stages, P.win_bytes, P.bm_words, P.tab_cap, P.pen);
   if (!dev->attr_set[dtype_idx]) {
     if (cudaFuncSetAttribute(fused_step_kernel<TL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              dev->smem_optin) != cudaSuccess)

@@ -48,7 +48,7 @@ constexpr int kMaxStagesWs = kMaxStages;          // full/empty barriers live in
 constexpr int kSlots = GR_WS_SLOTS;
 
 // Pieces after the common fixed layout (the penalty pieces are never used here).
-constexpr size_t kOffWin1 = kOffVar;                                      // slots 1.. child windows
+constexpr size_t kOffWin1 = kOffWin + align128(size_t(kWinBytes));       // slots 1.. child windows
 constexpr size_t kOffRec = kOffWin1 + (kSlots - 1) * align128(size_t(kWinBytes));   // records [kSlots][kMetaWords]
 constexpr size_t kOffPart = kOffRec + align128(kSlots * kMetaWords * 4);  // partial m, s [2][kSlots][kStrWarps]
 constexpr size_t kOffRowBars = kOffPart + align128(2 * kSlots * kStrWarps * 4);
