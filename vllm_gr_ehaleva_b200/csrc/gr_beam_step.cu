@@ -160,7 +160,7 @@ struct Scalars {
   uint64_t thr_key;
   uint64_t min_key;
   uint64_t tau_pref;
-  float lse_w[kWarps];         // streamed rows: each warp's log-sum-exp so far (cta_floor)
+  float lse_w[kWarps];         // streamed rows: each warp's log-sum-exp so far (cta_lse_bound)
   long long issued;
   int producer_done;
 #ifdef GR_PHASE_PROFILE
@@ -390,7 +390,7 @@ struct Step {
 
   // Process N consecutive columns starting at local column tb (x = raw values,
   // valid = lane holds real data).  Warp-uniform call.
-  // y_floor: streamed rows skip elements below it (-inf: none); see cta_floor().
+  // y_floor: streamed rows skip elements below it (-inf: none); see tau_floor().
   // lse = false: (m, s) already hold these columns; only the candidate part runs.
   template <int N>
   __device__ __forceinline__ void process(const RowCtx& c, const float* x, int tb, bool valid, float& m, float& s,
@@ -446,14 +446,12 @@ struct Step {
     }
   }
 
-  // Lowest y a streamed element needs to reach the request bound tau: its score
-  // cum + y - lse must be >= tau's score, and lse is at least the log-sum-exp of
-  // the columns seen so far.  Each warp publishes the log-sum-exp of the columns
-  // it has seen in lse_w (one float, reset to -inf at the row start); the other
-  // warps' values are at most one stage old and so still lower bounds of their
-  // final sums.  (m, s) are the calling thread's running max and sum.
-  // Warp-collective; -inf when there is no bound yet.
-  __device__ __forceinline__ float cta_floor(const RowCtx& c, uint64_t tau, float m, float s, float* lse_w) const {
+  // Log-sum-exp of the columns the CTA has seen so far, a lower bound of the
+  // row's.  Each warp publishes its own in lse_w (one float, reset to -inf at
+  // the row start); the other warps' values may be a few stages old and are
+  // still lower bounds of their final sums.  (m, s) are the calling thread's
+  // running max and sum.  Warp-collective; -inf when nothing is known yet.
+  __device__ __forceinline__ float cta_lse_bound(float m, float s, float* lse_w) const {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float M = m;
 #pragma unroll
@@ -461,12 +459,11 @@ struct Step {
     float t = (m == -kInf) ? 0.0f : s * fast_exp2((m - M) * kLog2e);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xFFFFFFFFu, t, o);
-    const float Lw = (M > -kInf && t > 0.0f && t < kInf) ? M + logf(t) : -kInf;
+    const float Lw = (M > -kInf && t > 0.0f && t < kInf) ? M + __logf(t) : -kInf;
     float Lo[kWarps];
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) Lo[w] = (w == warp) ? Lw : lse_w[w];
     if (lane == 0) lse_w[warp] = Lw;
-    if (tau == 0ull) return -kInf;
     float Lm = -kInf;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) Lm = fmaxf(Lm, Lo[w]);
@@ -474,9 +471,19 @@ struct Step {
     float tot = 0.0f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) tot += fast_exp2((Lo[w] - Lm) * kLog2e);
-    const float f = key_score(tau) - c.cum + (Lm + logf(tot));
+    return Lm + __logf(tot);
+  }
+
+  // Lowest y a streamed element needs to reach the request bound tau: its score
+  // cum + (y - lse) must reach tau's score, and lse >= L.  -inf without a bound.
+  __device__ __forceinline__ float tau_floor(const RowCtx& c, uint64_t tau, float L) const {
+    if (tau == 0ull || !(L > -kInf && L < kInf)) return -kInf;
+    const float ts = key_score(tau);
+    const float f = ts - c.cum + L;
     if (!(f > -kInf && f < kInf)) return -kInf;
-    return f - fabsf(f) * 1.0e-5f - 1e-30f;   // margin for y vs the exact quotient and the roundings
+    // margin for y vs the exact quotient, the approximate logarithms and the
+    // roundings of the score sum (relative to the magnitudes of its terms)
+    return f - 1.0e-5f * (fabsf(f) + fabsf(ts) + fabsf(c.cum) + fabsf(L)) - 1e-30f;
   }
 
   // ---- selection helpers ------------------------------------------------------
@@ -1353,8 +1360,10 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
         st.template process<1>(c, x, tl, valid, m, s, thr_y, thr_key);
       }
     }
-    // list length after the last complete append round (bounded rows)
+    // list length after the last complete append round, and the CTA's lse
+    // bound (bounded rows)
     uint32_t cnt_prev = 0;
+    float row_L = -kInf;
     if (bounded) {
       csync();
       cnt_prev = S.v->cnt;
@@ -1517,7 +1526,10 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
             }
           }
         }
-        const float floor_y = st.cta_floor(c, tau_use, m, s, S.v->lse_w);
+        // the CTA's lse bound: every stage at the row start, then every fourth
+        // (it grows by log(n / (n - 1)) per stage; a stale one is still a bound)
+        if (ch < 4 || (ch & 3) == 0) row_L = st.cta_lse_bound(m, s, S.v->lse_w);
+        const float floor_y = st.tau_floor(c, tau_use, row_L);
         const float thr_e = fmaxf(thr_y, floor_y);
         // survivors: bit j * EPV + i for element i of vector j
         uint32_t pm = 0;
@@ -1537,16 +1549,18 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
           }
         }
         const uint32_t cl = static_cast<uint32_t>(__popc(pm));
-        uint32_t inc = cl;
+        uint32_t inc = 0, base = 0;
+        if (__any_sync(0xFFFFFFFFu, cl != 0)) {
+          inc = cl;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
-          if (lane >= o) inc += t;
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+            if (lane >= o) inc += t;
+          }
+          const uint32_t wtot = __shfl_sync(0xFFFFFFFFu, inc, 31);
+          if (lane == 31) base = atomicAdd(&S.v->cnt, wtot);
+          base = __shfl_sync(0xFFFFFFFFu, base, 31);
         }
-        const uint32_t wtot = __shfl_sync(0xFFFFFFFFu, inc, 31);
-        uint32_t base = 0;
-        if (lane == 31 && wtot) base = atomicAdd(&S.v->cnt, wtot);
-        base = __shfl_sync(0xFFFFFFFFu, base, 31);
         csync();
         const uint32_t cnt_now = S.v->cnt;
         GR_PROF_VAL(12, cnt_now - cnt_prev);

@@ -520,8 +520,10 @@ __device__ void ws_finish_rows(const Params& P) {
         // row's lse exactly, so the bound needs no estimate of it
         float tau_off = -kInf;
         if (tau_seen) {
-          const float f = key_score(tau_seen) - c.cum + lse;
-          tau_off = f - fabsf(f) * 1.0e-5f - 1e-30f;   // margin for the roundings of the exact score
+          const float ts = key_score(tau_seen);
+          const float f = ts - c.cum + lse;
+          // margin for the roundings of the exact score (relative to its terms)
+          tau_off = f - 1.0e-5f * (fabsf(f) + fabsf(ts) + fabsf(c.cum) + fabsf(lse)) - 1e-30f;
         }
         tau_seen = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
         for (int vb = sb + warp * 32; vb < send; vb += kThreads) {
