@@ -157,6 +157,19 @@ def initial_state(wl, device):
     return cum, node, hist
 
 
+def step_kernel_name(wl) -> str:
+    """The step kernel the library picks for this workload: the warp-specialised
+    one unless GR_BEAM_KERNEL=stream or the step applies penalties in the
+    processed domain (those rows need the penalty table of the streaming kernel)."""
+    choice = os.environ.get("GR_BEAM_KERNEL", "auto")
+    cfg = wl["cfg"]
+    # step_kwargs passes the penalty lists in the processed mode; histories are non-empty
+    penalised = cfg["mode"] == "processed"
+    if choice == "stream" or (choice != "ws" and penalised):
+        return "fused_step_kernel"
+    return "fused_step_ws_kernel"
+
+
 def step_kwargs(wl):
     cfg = wl["cfg"]
     kw = dict(beam_width=wl["B"], csr=wl["csr_dev"], vocab_size=wl["V"])
@@ -268,6 +281,8 @@ def run_ours(args):
     steps_bytes = [bytes_cycle[i % levels] for i in range(args.steps)]
     avg_launch_ms = float(np.mean(per_step_ms))
     per_level_ms = [round(float(np.mean(per_step_ms[i::levels])), 5) for i in range(min(levels, args.steps))]
+    per_level_range = [[round(float(np.min(per_step_ms[i::levels])), 5), round(float(np.max(per_step_ms[i::levels])), 5)]
+                       for i in range(min(levels, args.steps))]
     achieved = float(np.mean([b / (ms * 1e-3) for b, ms in zip(steps_bytes, per_step_ms)])) / 1e9
     peak, peak_kind = peaks()
 
@@ -294,9 +309,10 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": None,
-                     "kernel": "gr::fused_step_ws_kernel (timed as the whole step: row_meta + fused + merge)",
+                     "kernel": f"gr::{step_kernel_name(wl)} (timed as the whole step: row_meta + fused + merge)",
                      "algorithmic_bytes_per_launch": int(np.mean(steps_bytes)),
                      "avg_launch_ms": round(avg_launch_ms, 5), "per_level_ms": per_level_ms,
+                     "per_level_ms_min_max": per_level_range,
                      "per_level_bytes": [int(b) for b in bytes_cycle]},
         "gpu_launches": 3 * args.steps,          # row_meta_kernel + fused_step_kernel + merge_kernel per step
         "clocks": clk,
