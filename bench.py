@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--requests", type=int, default=None, help="override requests per GPU")
+    ap.add_argument("--component", default="step", choices=["step", "suffix_kv"],
+                    help="suffix_kv: time the suffix KV gather of the attention pass instead of the step")
     return ap.parse_args()
 
 
@@ -577,8 +579,101 @@ def run_sharded(args):
     dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------ suffix KV gather
+def suffix_layout(R, B, shared, steps, rng):
+    """slot_mapping / slot_mapping_out of R mega-decode requests laid out as
+    the reference's metadata builder does (beam_attn.py:319-413): per request
+    `shared` uncached prefix tokens plus B beams x `steps` decode tokens; beam 0's
+    suffix is its own tokens (prefix tail included), beam b > 0 reads the prefix
+    tail then its own.  Slots are a random permutation of the cache."""
+    per_req = shared + B * steps
+    n_src = R * per_req
+    smo = []
+    for r in range(R):
+        base = r * per_req
+        smo.extend(range(base, base + shared + steps))
+        for b in range(1, B):
+            smo.extend(range(base, base + shared))
+            own = base + shared + b * steps
+            smo.extend(range(own, own + steps))
+    return n_src, np.asarray(smo, np.int32)
+
+
+def run_suffix_kv(args):
+    import torch
+    from vllm_gr_ehaleva_b200.attention import extract_suffix_kv
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    R, B, H, D, block = 64, 128, 8, 128, 16
+    rng = np.random.default_rng(7)
+    lines = []
+    for name, shared in (("decode", 0), ("shared_tail", 24)):
+        steps = 8
+        n_src, smo_np = suffix_layout(R, B, shared, steps, rng)
+        n_slots = ((n_src + block - 1) // block) * block
+        slots = torch.from_numpy(rng.permutation(n_slots)[:n_src].astype(np.int64)).to(device)
+        smo = torch.from_numpy(smo_np).to(device)
+        n = int(smo.numel())
+        k = torch.randn(n_slots // block, block, H, D, device=device).to(torch.bfloat16)
+        v = torch.randn(n_slots // block, block, H, D, device=device).to(torch.bfloat16)
+        row = H * D * 2
+        moved = 2 * n * row * 2                 # K and V rows, each read once and written once
+        hbm = 2 * (n_src + n) * row             # distinct source rows read + rows written (shared rows hit L2)
+        stream = torch.cuda.current_stream(device)
+
+        def timed(fn, iters):
+            for _ in range(max(args.warmup, 3)):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(iters):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / iters
+
+        iters = min(args.steps, 200)
+        ms = timed(lambda: extract_suffix_kv(k, v, slots, smo, n), iters)
+        flat_k, flat_v = k.view(-1, H, D), v.view(-1, H, D)
+        ms_torch = timed(lambda: (flat_k[slots[smo.long()]], flat_v[slots[smo.long()]]), iters)
+        ok, ov = extract_suffix_kv(k, v, slots, smo, n)
+        exact = bool(torch.equal(ok, flat_k[slots[smo.long()]]) and torch.equal(ov, flat_v[slots[smo.long()]]))
+        # CPU baseline: the oracle's NumPy gather on a bounded sample of the same layout
+        from oracle import suffix_kv as osk
+        ns = min(n, 8192)
+        kc, vc = k.float().cpu().numpy(), v.float().cpu().numpy()
+        sm_np = slots.cpu().numpy()
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 2.0:
+            osk.gather(kc, vc, sm_np, smo_np, ns)
+            reps += 1
+        cpu_gbs = reps * 2 * ns * row * 2 / (time.perf_counter() - t0) / 1e9
+        peak, peak_kind = peaks()
+        gbs = moved / (ms * 1e-3) / 1e9
+        hbm_gbs = hbm / (ms * 1e-3) / 1e9
+        lines.append({
+            "metric": "suffix KV gather bytes moved per second", "layout": name, "value": round(gbs, 1),
+            "unit": "GB/s", "ms_per_call": round(ms, 5), "tokens": n, "bytes_per_call": moved,
+            "exact_vs_torch_index": exact, "torch_index_gbs": round(moved / (ms_torch * 1e-3) / 1e9, 1),
+            "dtype": "bf16", "config": {"requests": R, "beams": B, "shared_tail": shared, "steps": steps,
+                                         "kv_heads": H, "head_dim": D, "block_size": block,
+                                         "l2": "cache and outputs larger than L2, no flush"},
+            "roofline": {"bound": "hbm", "achieved": round(hbm_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(hbm_gbs / peak, 4), "peak_kind": peak_kind, "hbm_bytes_per_call": hbm},
+            "cpu_baseline": {"value": round(cpu_gbs, 2), "unit": "GB/s", "cores": 1, "kind": "port",
+                             "sample": f"{ns} tokens (oracle/suffix_kv.py NumPy gather, fp32 copy of the cache)"},
+        })
+    for line in lines:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.component == "suffix_kv":
+        run_suffix_kv(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     elif "shards" in CONFIGS[args.config] and int(os.environ.get("WORLD_SIZE", "1")) > 1:

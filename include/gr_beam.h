@@ -213,6 +213,40 @@ int32_t gr_merge_candidates(const gr_step_desc* desc, const gr_step_io* io,
                             const uint64_t* gathered_keys, int32_t num_shards,
                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- suffix KV gather for the beam-consecutive attention pass -------------
+ *
+ * The beams of a mega-request attend to the shared prefix through the paged
+ * KV cache and to their own suffix (the uncached prefix tail plus the tokens
+ * decoded since the fork) through a contiguous copy.  This gathers that copy:
+ * for every output token t
+ *     src  = slot_mapping_out[t]                       (index into slot_mapping)
+ *     slot = slot_mapping[src]                         (flat cache slot)
+ *     out_k[t, h, d] = k_cache[slot * k_stride_tok + h * k_stride_head + d * k_stride_dim]
+ * and the same for V.  Strides are in elements; out_k / out_v are contiguous
+ * [num_out][num_heads][head_dim].  A flat slot is block * block_size + offset
+ * (vLLM's layout with the blocks contiguous, so the token stride applies).
+ * Sources outside [0, num_src) or slots outside [0, num_slots) produce zero
+ * rows and set GR_DEVERR_BAD_SLOT in *err (err may be NULL).
+ * Replaces vllm_gr/v1/attention/backends/beam_attn.py:62-117
+ * (paged_kv_to_contig_suffix_kernel, extract_suffix_kv). */
+#define GR_DEVERR_BAD_SLOT      0x20  /* suffix gather: source or slot out of range */
+
+typedef struct gr_kv_gather_desc {
+  int64_t num_out;          /* output tokens (slot_mapping_out entries)          */
+  int64_t num_src;          /* slot_mapping entries                              */
+  int64_t num_slots;        /* cache slots (num_blocks * block_size)             */
+  int32_t num_heads;        /* KV heads                                          */
+  int32_t head_dim;         /* elements per head                                 */
+  int32_t elem_bytes;       /* 1, 2 or 4                                         */
+  int32_t reserved;
+  int64_t k_stride_tok, k_stride_head, k_stride_dim;
+  int64_t v_stride_tok, v_stride_head, v_stride_dim;
+} gr_kv_gather_desc;
+
+int32_t gr_suffix_kv_gather(const gr_kv_gather_desc* desc, const void* k_cache, const void* v_cache,
+                            const int64_t* slot_mapping, const int32_t* slot_mapping_out,
+                            void* out_k, void* out_v, int32_t* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -117,6 +117,89 @@ def install(reference_root: str) -> None:
         vmm.MultiModalDataDict = dict
 
 
+def install_attention(reference_root: str) -> None:
+    """Make the reference's beam attention backend importable on a CPU-only
+    host with the installed vLLM: stand-ins for the four names it imports that
+    this vLLM does not have (is_quantized_kv_cache, flash_attn_supports_fp8,
+    vllm_is_batch_invariant: constant False; AttentionMetadataBuilder: an empty
+    generic base).  Only its metadata builder (plain Python) is used."""
+    install(reference_root)
+    import typing
+    import vllm.model_executor.layers.batch_invariant as bi
+    import vllm.v1.attention.backend as vb
+    import vllm.v1.attention.backends.fa_utils as fu
+    import vllm.v1.attention.backends.utils as vu
+    if not hasattr(vb, "is_quantized_kv_cache"):
+        vb.is_quantized_kv_cache = lambda *a, **k: False
+    if not hasattr(fu, "flash_attn_supports_fp8"):
+        fu.flash_attn_supports_fp8 = lambda *a, **k: False
+    if not hasattr(bi, "vllm_is_batch_invariant"):
+        bi.vllm_is_batch_invariant = lambda *a, **k: False
+    if not hasattr(vu, "AttentionMetadataBuilder"):
+        T = typing.TypeVar("T")
+
+        class AttentionMetadataBuilder(typing.Generic[T]):
+            pass
+
+        vu.AttentionMetadataBuilder = AttentionMetadataBuilder
+
+
+def reference_suffix_metadata(reference_root: str, *, num_reqs, beam_width, q_seq_len, prefix_len, steps,
+                              cache_len, block_size, block_tables, slot_mapping):
+    """Run the reference's BeamAttentionMetadataBuilder.build (beam_attn.py:480-559)
+    for mega-decode requests laid out as in its own kernel test
+    (tests/kernels/attention/test_cascade_beam_flash_attn.py:322-380) and return
+    the suffix-pass metadata it builds."""
+    install_attention(reference_root)
+    import torch
+    from vllm_gr.v1.attention.backends.beam_attn import MEGA_DATA_VAR, BeamAttentionMetadataBuilder
+
+    class Common:
+        pass
+
+    cm = Common()
+    cm.num_reqs = num_reqs
+    cm.query_start_loc_cpu = torch.arange(0, (num_reqs * beam_width + 1) * q_seq_len, beam_width * q_seq_len,
+                                          dtype=torch.int32)
+    cm.query_start_loc = cm.query_start_loc_cpu
+    cm.seq_lens = torch.full((num_reqs,), prefix_len + beam_width * steps, dtype=torch.int32)
+    cm.block_table_tensor = block_tables
+    cm.num_actual_tokens = num_reqs * beam_width * q_seq_len
+    cm.max_query_len = q_seq_len * beam_width
+    cm.max_seq_len = prefix_len + beam_width * steps
+    cm.causal = True
+    cm.slot_mapping = slot_mapping
+    info = {"mega_data": {f"req_{i}": {"is_mega_decode": True, "prefix_len": prefix_len,
+                                       "mega_beam_width": beam_width, "mega_decode_steps": steps,
+                                       "cache_len": cache_len} for i in range(num_reqs)},
+            "req_ids": [f"req_{i}" for i in range(num_reqs)]}
+    token = MEGA_DATA_VAR.set(info)
+    try:
+        b = BeamAttentionMetadataBuilder.__new__(BeamAttentionMetadataBuilder)
+        b.device = "cpu"
+        b.block_size = block_size
+        b.aot_schedule = False
+        b.aot_sliding_window = None
+        b.use_full_cuda_graph = False
+        b.max_cudagraph_size = None
+        b.max_num_splits = 0
+        m = b.build(common_prefix_len=prefix_len, common_attn_metadata=cm, fast_build=False)
+    finally:
+        MEGA_DATA_VAR.reset(token)
+
+    def lst(x):
+        return None if x is None else x.tolist()
+
+    return {
+        "mega_prefix_indices": lst(m.mega_prefix_indices),
+        "suffix_slot_mapping_out": lst(m.mega_suffix_slot_mapping_out),
+        "suffix_total_tokens": int(m.mega_suffix_total_tokens),
+        "suffix_seq_lens": lst(m.mega_suffix_seq_lens),
+        "suffix_cu_seqlens_q": lst(m.mega_suffix_cu_seqlens_q),
+        "suffix_cu_seqlens_k": lst(m.mega_suffix_cu_seqlens_k),
+    }
+
+
 # ---------------------------------------------------------------- mock sampler
 def beam_logits(tokens, vocab: int, sigma: float, seed: int, bf16: bool) -> np.ndarray:
     """float32 logits of one beam, a function of its whole token sequence."""

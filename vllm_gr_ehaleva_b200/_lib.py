@@ -18,7 +18,7 @@ STATUS_NAMES = {
 }
 DEVERR_NAMES = {
     0x1: "GR_DEVERR_BAD_NODE", 0x2: "GR_DEVERR_BAD_CHILD", 0x4: "GR_DEVERR_TIMEOUT",
-    0x8: "GR_DEVERR_OVERFLOW", 0x10: "GR_DEVERR_TIE_BOUNDARY",
+    0x8: "GR_DEVERR_OVERFLOW", 0x10: "GR_DEVERR_TIE_BOUNDARY", 0x20: "GR_DEVERR_BAD_SLOT",
 }
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 LOGPROBS_RAW, LOGPROBS_PROCESSED = 0, 1
@@ -27,6 +27,7 @@ NODE_UNCONSTRAINED, NODE_DEAD = -1, -2
 EXPORTED_SYMBOLS = (
     "gr_abi_version", "gr_status_string", "gr_beam_step_workspace_size", "gr_beam_step",
     "gr_lse_partials", "gr_shard_candidates", "gr_merge_candidates", "gr_beam_step_noalloc",
+    "gr_suffix_kv_gather",
 )
 NOALLOC_SCRATCH_BYTES = 16 << 20
 
@@ -59,6 +60,24 @@ _IO_FIELDS = (
 
 class StepIO(ctypes.Structure):
     _fields_ = [(name, ctypes.c_void_p) for name in _IO_FIELDS]
+
+
+class KvGatherDesc(ctypes.Structure):
+    _fields_ = [
+        ("num_out", ctypes.c_int64),
+        ("num_src", ctypes.c_int64),
+        ("num_slots", ctypes.c_int64),
+        ("num_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("elem_bytes", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("k_stride_tok", ctypes.c_int64),
+        ("k_stride_head", ctypes.c_int64),
+        ("k_stride_dim", ctypes.c_int64),
+        ("v_stride_tok", ctypes.c_int64),
+        ("v_stride_head", ctypes.c_int64),
+        ("v_stride_dim", ctypes.c_int64),
+    ]
 
 
 def describe_deverr(code: int) -> str:
@@ -98,6 +117,10 @@ def load(path: str | None = None) -> ctypes.CDLL:
     lib.gr_merge_candidates.restype = ctypes.c_int32
     lib.gr_merge_candidates.argtypes = [P(StepDesc), P(StepIO), ctypes.c_void_p, ctypes.c_int32,
                                         ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.gr_suffix_kv_gather.restype = ctypes.c_int32
+    lib.gr_suffix_kv_gather.argtypes = [P(KvGatherDesc), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_void_p]
     _lib = lib
     return lib
 

@@ -1,22 +1,30 @@
 // gr_beam_step.cu — fused constrained beam-search step for B200 (sm_100a).
 //
-// One persistent CTA per SM walks a strided list of logit rows (one row =
-// one beam of one request).  For each row it
-//   (a) streams the row through a ring of shared-memory stages filled by
-//       cp.async.bulk (TMA bulk copies, one elected thread, mbarrier
-//       completion) while all 512 threads keep an online max / sum-exp
-//       (vLLM's full-vocab log_softmax normaliser, sampler.py:300-301);
-//   (b) keeps a shared-memory copy of the token window that holds the row's
-//       trie children (constrained beams), or a thresholded top-k of the
-//       streamed values (unconstrained / reference-literal beams);
-//   (c) after the row's log-sum-exp is known, scores its candidates
-//       score = cum + (y - lse) (serving_engine.py:511, 533), drops those
-//       below the request's running 2B-th best key, selects at most 2B and
-//       appends them to the request's candidate buffer;
-//   (d) the CTA that finishes a request's last row merges the request's
-//       candidates into the canonical top-2B, the new beams (parent, token,
-//       child node) and the forked token table (serving_engine.py:566-590).
-// No CTA ever waits for another one; every mbarrier wait is bounded.
+// A step is three kernels on the caller's stream:
+//   row_meta_kernel   one thread per row (one row = one beam of one request):
+//                     the row's 128-byte record (node, cum, CSR range, child
+//                     tokens of small nodes, temperature) and the per-step
+//                     resets (request bound, list lengths);
+//   step kernel       persistent CTAs walk the rows: every logit row is streamed
+//                     once through a ring of shared-memory stages filled by
+//                     cp.async.bulk (one elected thread, mbarrier completion)
+//                     while the consumer warps keep an online max / sum-exp
+//                     (vLLM's full-vocab log_softmax normaliser,
+//                     sampler.py:300-301); the row's candidates (trie children
+//                     from a shared-memory copy of the row's child window, or
+//                     a bounded top-k of the streamed values) are scored
+//                     score = cum + (y - lse) (serving_engine.py:511, 533),
+//                     filtered against the request's running 2B-th best key,
+//                     cut to 2B and appended to the request's candidate list.
+//                     Two kernels: fused_step_ws_kernel (gr_step_ws.cuh, warp-
+//                     specialised producer / streaming / row-end warps) and
+//                     fused_step_kernel below (all consumer warps do every
+//                     phase; penalties and reference-literal top-K);
+//   merge_kernel      one CTA per request: the canonical top-2B of its list,
+//                     the new beams, child nodes and the forked token table
+//                     (serving_engine.py:566-590).
+// Kernels wait for one another only through stream order (programmatic
+// dependent launch overlaps prologues); every mbarrier wait is bounded.
 
 #include <cstdint>
 #include <cstdio>
