@@ -8,9 +8,11 @@
 // (vllm_gr/v1/attention/backends/beam_attn.py:62-117).
 //
 // Here the copy is HBM-bound data movement, laid out for it:
-//   * a warp owns 32 output tokens at a time: each lane resolves one token's
-//     index chain (two dependent loads), so the 64 index loads of the batch are
-//     in flight together instead of two round trips per token;
+//   * a warp owns 32 output tokens at a time (batches dealt round robin over
+//     the grid's warps, CTA-fastest, so the load stays even over the SMs): each
+//     lane resolves one token's index chain (two dependent loads), so the 64
+//     index loads of the batch are in flight together instead of two round
+//     trips per token;
 //   * the warp then copies the batch two tokens at a time, K and V rows of both
 //     in one unrolled group of 16-byte loads (all issued before the first
 //     store), so each lane keeps up to 16 x 16 B in flight;
@@ -72,13 +74,19 @@ __device__ __forceinline__ int64_t resolve_slot(const Params& P, int64_t t, bool
   return slot;
 }
 
+// Output tokens go to warps in batches of 32, round robin over the grid's warps
+// numbered CTA-fastest: consecutive batches run on different SMs at once, and a
+// grid with more warps than batches leaves its idle warps spread over all SMs.
+__device__ __forceinline__ int64_t warp_id_spread() {
+  return static_cast<int64_t>(threadIdx.x >> 5) * gridDim.x + blockIdx.x;
+}
+
 __global__ void __launch_bounds__(kThreads) gather_rows_kernel(const Params P) {
   const int lane = threadIdx.x & 31;
-  const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
-  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarps;
   const int nvec = P.nvec;
   const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-  for (int64_t t0 = warp * 32; t0 < P.num_out; t0 += nwarps * 32) {
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarps;
+  for (int64_t t0 = warp_id_spread() * 32; t0 < P.num_out; t0 += nwarps * 32) {
     const int nb = static_cast<int>(min(static_cast<int64_t>(32), P.num_out - t0));
     bool bad = false;
     int64_t slot = -1;
@@ -126,14 +134,13 @@ __global__ void __launch_bounds__(kThreads) gather_rows_kernel(const Params P) {
 template <typename E>
 __global__ void __launch_bounds__(kThreads) gather_elems_kernel(const Params P) {
   const int lane = threadIdx.x & 31;
-  const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
-  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarps;
   const int row = P.heads * P.dim;
   const E* K = reinterpret_cast<const E*>(P.k);
   const E* V = reinterpret_cast<const E*>(P.v);
   E* OK = reinterpret_cast<E*>(P.out_k);
   E* OV = reinterpret_cast<E*>(P.out_v);
-  for (int64_t t0 = warp * 32; t0 < P.num_out; t0 += nwarps * 32) {
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarps;
+  for (int64_t t0 = warp_id_spread() * 32; t0 < P.num_out; t0 += nwarps * 32) {
     const int nb = static_cast<int>(min(static_cast<int64_t>(32), P.num_out - t0));
     bool bad = false;
     int64_t slot = -1;
@@ -215,8 +222,8 @@ extern "C" int32_t gr_suffix_kv_gather(const gr_kv_gather_desc* d, const void* k
                    d->v_stride_head == d->head_dim && row_bytes % 16 == 0 && row_bytes / 16 < (1ll << 30) &&
                    P.k_tok_bytes % 16 == 0 && P.v_tok_bytes % 16 == 0 && aligned(k_cache) && aligned(v_cache) &&
                    aligned(out_k) && aligned(out_v);
-  const int64_t batches = (d->num_out + 31) / 32;
-  const int64_t want = (batches + kWarps - 1) / kWarps;
+  // at least ~8 tokens per warp, then every resident CTA
+  const int64_t want = (d->num_out + 8 * kWarps - 1) / (8 * kWarps);
   // a persistent grid: every CTA resident at once
   const int64_t cap = static_cast<int64_t>(g_dev[dev].sms) * (vec ? g_dev[dev].occ_rows : g_dev[dev].occ_elems);
   const int grid = static_cast<int>(want < cap ? want : cap);
