@@ -33,7 +33,10 @@ namespace grkv {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kUnroll = 4;   // 16-byte vectors per lane per row copy and group
+#ifndef GR_KV_UNROLL
+#define GR_KV_UNROLL 4
+#endif
+constexpr int kUnroll = GR_KV_UNROLL;   // 16-byte vectors per lane per row copy and group
 
 struct Params {
   const unsigned char* k;
