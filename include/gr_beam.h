@@ -247,6 +247,49 @@ int32_t gr_suffix_kv_gather(const gr_kv_gather_desc* desc, const void* k_cache, 
                             const int64_t* slot_mapping, const int32_t* slot_mapping_out,
                             void* out_k, void* out_v, int32_t* err, void* stream);
 
+/* Suffix-pass metadata of mega-decode requests, built on the device.
+ *
+ * The host keeps the per-request arithmetic of the reference builder (O(1) per
+ * request) and passes one record per request that takes part in the pass, in
+ * request order (`reqs` is a device array).  The call writes the per-beam and
+ * per-token arrays the reference builds in Python loops
+ * (beam_attn.py:319-413, 432-476).  With own_b the query tokens of beam b
+ * (own_0 = own0; for b >= 1 min(steps, own_total - own0 - (b-1)*steps)) and
+ * its suffix length seq_b (own0 for beam 0, remaining + own_b otherwise):
+ *   prefix_indices[out_base + i] = q_start + i                 for i < own_total
+ *   slot_mapping_out[suffix_base + sum_{c<b} seq_c + j]       for j < seq_b:
+ *       beam 0:  out_base + j
+ *       beam b:  out_base + j                                    (j < remaining)
+ *                out_base + own0 + (b-1)*steps + (j - remaining) (otherwise)
+ *   cu_seqlens_q[beam_base + b + 1] = out_base + sum_{c<=b} own_c
+ *   cu_seqlens_k[beam_base + b + 1] = suffix_base + sum_{c<=b} seq_c
+ *   cu_seqlens_q[0] = cu_seqlens_k[0] = 0
+ * out_base / suffix_base / beam_base are the running totals of own_total /
+ * sum seq / beams over the earlier records.  Replaces, for the suffix pass,
+ * BeamAttentionMetadataBuilder._build_mega_mappings and the tensors made from
+ * its lists in _create_mega_tensors. */
+typedef struct gr_suffix_req {
+  int64_t q_start;       /* first query token of the request's mega part         */
+  int64_t out_base;      /* its first position in the mega token order             */
+  int64_t suffix_base;   /* its first entry in slot_mapping_out                    */
+  int32_t beam_base;     /* its first beam in the cu_seqlens arrays                */
+  int32_t beams;         /* active beams (beam 0 included), >= 1                   */
+  int32_t remaining;     /* uncached prefix tokens (beam 0's first ones)           */
+  int32_t steps;         /* decode steps per beam, >= 1                            */
+  int32_t own0;          /* beam 0's query tokens, >= 1                            */
+  int32_t own_total;     /* all query tokens of the request's mega part            */
+} gr_suffix_req;
+
+#define GR_DEVERR_BAD_RECORD    0x40  /* suffix metadata: a record points outside the outputs */
+
+/* prefix_indices has total_prefix entries, slot_mapping_out total_suffix, the
+ * cu_seqlens arrays total_beams + 1.  Writes a record would place outside them
+ * are dropped and set GR_DEVERR_BAD_RECORD in *err (err may be NULL). */
+int32_t gr_suffix_metadata(const gr_suffix_req* reqs, int32_t num_reqs, int64_t total_beams,
+                           int64_t total_prefix, int64_t total_suffix, int64_t* prefix_indices,
+                           int32_t* slot_mapping_out, int32_t* cu_seqlens_q, int32_t* cu_seqlens_k,
+                           int32_t* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -70,3 +70,74 @@ def test_wrapper_rejects_bad_arguments():
     kv = torch.zeros(2, 2, 16, 2, 64, dtype=torch.bfloat16)
     d = suffix_kv.gather_desc(kv[:, 0], kv[:, 1], sm, smo, 3)
     assert d.k_stride_tok == 128 and d.num_slots <= 2 * 16
+
+
+def _expand(recs, tot):
+    """The arrays gr_suffix_metadata writes, from its records (the formulas of
+    its declaration in include/gr_beam.h), in NumPy."""
+    pi = np.zeros(tot["prefix"], np.int64)
+    smo = np.zeros(tot["suffix"], np.int32)
+    cu_q = np.zeros(tot["beams"] + 1, np.int32)
+    cu_k = np.zeros(tot["beams"] + 1, np.int32)
+    for (q_start, out_base, suffix_base, beam_base, beams, remaining, steps, own0, own_total) in recs:
+        pi[out_base:out_base + own_total] = q_start + np.arange(own_total)
+        k = suffix_base
+        q = out_base
+        for b in range(beams):
+            own = own0 if b == 0 else min(steps, own_total - own0 - (b - 1) * steps)
+            if b == 0:
+                vals = out_base + np.arange(own0)
+            else:
+                vals = np.concatenate([out_base + np.arange(remaining),
+                                       out_base + own0 + (b - 1) * steps + np.arange(own)])
+            smo[k:k + len(vals)] = vals
+            k += len(vals)
+            q += own
+            cu_q[beam_base + b + 1] = q
+            cu_k[beam_base + b + 1] = k
+    return pi, smo, cu_q, cu_k
+
+
+@pytest.mark.parametrize("idx", range(len(_cases())))
+def test_device_metadata_records_match_reference(idx):
+    from vllm_gr_ehaleva_b200.attention import suffix_records
+    c = _cases()[idx]
+    mega = [dict(prefix_len=c["prefix_len"], cache_len=0, beam_width=c["beam_width"], steps=c["suffix_kv_len"])
+            ] * c["batch_size"]
+    recs, tot = suffix_records(mega, _q_starts(c), c["block_size"])
+    assert tot["suffix"] == c["suffix_total_tokens"]
+    if tot["suffix"] == 0:
+        return
+    pi, smo, cu_q, cu_k = _expand(recs, tot)
+    np.testing.assert_array_equal(pi, np.asarray(c["mega_prefix_indices"]))
+    np.testing.assert_array_equal(smo, np.asarray(c["suffix_slot_mapping_out"]))
+    np.testing.assert_array_equal(cu_q, np.asarray(c["suffix_cu_seqlens_q"]))
+    np.testing.assert_array_equal(cu_k, np.asarray(c["suffix_cu_seqlens_k"]))
+    assert tot["max_k"] == max(c["suffix_seq_lens"])
+
+
+def test_records_mixed_requests_match_oracle():
+    # standard requests between mega ones, a long uncached prefix, budgets that cut beams short
+    from vllm_gr_ehaleva_b200.attention import suffix_records
+    rng = np.random.default_rng(5)
+    for _ in range(40):
+        n = int(rng.integers(1, 7))
+        q_lens = rng.integers(0, 200, n)
+        q_starts = [0] + np.cumsum(q_lens).tolist()
+        mega = []
+        for i in range(n):
+            if rng.random() < 0.25:
+                mega.append(None)
+                continue
+            prefix = int(rng.integers(0, 80))
+            mega.append(dict(prefix_len=prefix, cache_len=int(rng.integers(0, prefix + 1)),
+                             beam_width=int(rng.integers(0, 9)), steps=int(rng.integers(0, 6))))
+        block = int(rng.choice([16, 32]))
+        pi, smo, q_l, seq_l = osk.suffix_metadata(mega, q_starts, block)
+        recs, tot = suffix_records(mega, q_starts, block)
+        e_pi, e_smo, e_cq, e_ck = _expand(recs, tot)
+        np.testing.assert_array_equal(e_pi, pi)
+        np.testing.assert_array_equal(e_smo, smo)
+        np.testing.assert_array_equal(np.diff(e_cq), q_l)
+        np.testing.assert_array_equal(np.diff(e_ck), seq_l)
+        assert tot["max_q"] == (max(q_l) if len(q_l) else 0) and tot["max_k"] == (max(seq_l) if len(seq_l) else 0)

@@ -153,3 +153,62 @@ def test_large_gather():
     ok, ov = extract_suffix_kv(k, v, sm, smo, 65537)
     ek, ev = _expected(k, v, sm, smo, 65537)
     assert torch.equal(ok, ek) and torch.equal(ov, ev)
+
+
+def _q_starts(c):
+    per = c["beam_width"] * c["q_seq_len"]
+    return list(range(0, per * c["batch_size"] + 1, per))
+
+
+def test_device_metadata_matches_reference_builder():
+    from vllm_gr_ehaleva_b200.attention import build_suffix_metadata
+    for c in _golden():
+        mega = [dict(prefix_len=c["prefix_len"], cache_len=0, beam_width=c["beam_width"],
+                     steps=c["suffix_kv_len"])] * c["batch_size"]
+        err = torch.zeros(1, dtype=torch.int32, device=DEV)
+        m = build_suffix_metadata(mega, _q_starts(c), c["block_size"], DEV, err=err)
+        assert m["suffix_total_tokens"] == c["suffix_total_tokens"]
+        assert m["mega_prefix_indices"].cpu().tolist() == c["mega_prefix_indices"]
+        assert m["suffix_slot_mapping_out"].cpu().tolist() == c["suffix_slot_mapping_out"]
+        assert m["suffix_cu_seqlens_q"].cpu().tolist() == c["suffix_cu_seqlens_q"]
+        assert m["suffix_cu_seqlens_k"].cpu().tolist() == c["suffix_cu_seqlens_k"]
+        assert m["suffix_seq_lens"].cpu().tolist() == c["suffix_seq_lens"]
+        assert int(err.item()) == 0
+
+
+def test_device_metadata_random_layouts_match_oracle():
+    from vllm_gr_ehaleva_b200.attention import build_suffix_metadata
+    rng = np.random.default_rng(9)
+    for _ in range(30):
+        n = int(rng.integers(1, 40))
+        q_lens = rng.integers(0, 600, n)
+        q_starts = [0] + np.cumsum(q_lens).tolist()
+        mega = [None if rng.random() < 0.2 else
+                dict(prefix_len=int(p), cache_len=int(rng.integers(0, p + 1)), beam_width=int(rng.integers(0, 65)),
+                     steps=int(rng.integers(0, 9))) for p in rng.integers(0, 100, n)]
+        block = int(rng.choice([16, 32]))
+        pi, smo, q_l, seq_l = osk.suffix_metadata(mega, q_starts, block)
+        m = build_suffix_metadata(mega, q_starts, block, DEV)
+        np.testing.assert_array_equal(m["mega_prefix_indices"].cpu().numpy(), pi)
+        np.testing.assert_array_equal(m["suffix_slot_mapping_out"].cpu().numpy(), smo)
+        np.testing.assert_array_equal(np.diff(m["suffix_cu_seqlens_q"].cpu().numpy()), q_l)
+        np.testing.assert_array_equal(m["suffix_seq_lens"].cpu().numpy(), seq_l)
+
+
+def test_device_metadata_rejects_inconsistent_records():
+    # a record that points past the outputs: its writes are dropped and flagged
+    import ctypes
+    lib = _lib.load()
+    rec = (_lib.SuffixReq * 1)(_lib.SuffixReq(0, 50, 0, 0, 2, 3, 4, 7, 11))   # out_base 50 > 11 prefix entries
+    recs = torch.frombuffer(bytearray(bytes(rec)), dtype=torch.uint8).to(DEV)
+    pi = torch.full((11,), -7, dtype=torch.int64, device=DEV)
+    smo = torch.full((17,), -7, dtype=torch.int32, device=DEV)
+    cq = torch.full((3,), -7, dtype=torch.int32, device=DEV)
+    ck = torch.full((3,), -7, dtype=torch.int32, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    rc = lib.gr_suffix_metadata(recs.data_ptr(), 1, 2, 11, 17, pi.data_ptr(), smo.data_ptr(), cq.data_ptr(),
+                                ck.data_ptr(), err.data_ptr(), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) & 0x40
+    assert (pi == -7).all() and (smo == -7).all()

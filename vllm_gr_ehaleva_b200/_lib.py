@@ -19,6 +19,7 @@ STATUS_NAMES = {
 DEVERR_NAMES = {
     0x1: "GR_DEVERR_BAD_NODE", 0x2: "GR_DEVERR_BAD_CHILD", 0x4: "GR_DEVERR_TIMEOUT",
     0x8: "GR_DEVERR_OVERFLOW", 0x10: "GR_DEVERR_TIE_BOUNDARY", 0x20: "GR_DEVERR_BAD_SLOT",
+    0x40: "GR_DEVERR_BAD_RECORD",
 }
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 LOGPROBS_RAW, LOGPROBS_PROCESSED = 0, 1
@@ -27,7 +28,7 @@ NODE_UNCONSTRAINED, NODE_DEAD = -1, -2
 EXPORTED_SYMBOLS = (
     "gr_abi_version", "gr_status_string", "gr_beam_step_workspace_size", "gr_beam_step",
     "gr_lse_partials", "gr_shard_candidates", "gr_merge_candidates", "gr_beam_step_noalloc",
-    "gr_suffix_kv_gather",
+    "gr_suffix_kv_gather", "gr_suffix_metadata",
 )
 NOALLOC_SCRATCH_BYTES = 16 << 20
 
@@ -60,6 +61,20 @@ _IO_FIELDS = (
 
 class StepIO(ctypes.Structure):
     _fields_ = [(name, ctypes.c_void_p) for name in _IO_FIELDS]
+
+
+class SuffixReq(ctypes.Structure):
+    _fields_ = [
+        ("q_start", ctypes.c_int64),
+        ("out_base", ctypes.c_int64),
+        ("suffix_base", ctypes.c_int64),
+        ("beam_base", ctypes.c_int32),
+        ("beams", ctypes.c_int32),
+        ("remaining", ctypes.c_int32),
+        ("steps", ctypes.c_int32),
+        ("own0", ctypes.c_int32),
+        ("own_total", ctypes.c_int32),
+    ]
 
 
 class KvGatherDesc(ctypes.Structure):
@@ -121,6 +136,10 @@ def load(path: str | None = None) -> ctypes.CDLL:
     lib.gr_suffix_kv_gather.argtypes = [P(KvGatherDesc), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                         ctypes.c_void_p]
+    lib.gr_suffix_metadata.restype = ctypes.c_int32
+    lib.gr_suffix_metadata.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
+                                       ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     _lib = lib
     return lib
 

@@ -165,6 +165,65 @@ __global__ void __launch_bounds__(kThreads) gather_elems_kernel(const Params P) 
   }
 }
 
+// ---- suffix-pass metadata -------------------------------------------------
+// One warp per beam of the pass: the beam's request by binary search over the
+// records' beam_base, then the beam's stretch of each output array from the
+// closed forms of the reference builder's loop (beam_attn.py:319-413): beam 0
+// takes min(q_len, remaining + steps) query tokens, every later beam `steps`
+// until the request's query budget runs out.
+struct MetaParams {
+  const gr_suffix_req* reqs;
+  int num_reqs;
+  int64_t total_beams, total_prefix, total_suffix;
+  int64_t* prefix_indices;
+  int32_t* smo;
+  int32_t* cu_q;
+  int32_t* cu_k;
+  int32_t* err;
+};
+
+__global__ void __launch_bounds__(kThreads) suffix_metadata_kernel(const MetaParams M) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarps;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    M.cu_q[0] = 0;
+    M.cu_k[0] = 0;
+  }
+  for (int64_t gb = warp_id_spread(); gb < M.total_beams; gb += nwarps) {
+    int lo = 0, hi = M.num_reqs - 1;   // last record with beam_base <= gb
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (static_cast<int64_t>(M.reqs[mid].beam_base) <= gb) lo = mid; else hi = mid - 1;
+    }
+    const gr_suffix_req R = M.reqs[lo];
+    const int64_t b = gb - R.beam_base;
+    bool bad = b < 0 || b >= R.beams || R.out_base < 0 || R.suffix_base < 0 || R.remaining < 0 || R.steps < 1 ||
+               R.own0 < 1 || R.own_total < R.own0;
+    const int64_t extra = static_cast<int64_t>(R.own_total) - R.own0;   // query tokens of beams 1..
+    const int64_t before = (b == 0) ? 0 : min((b - 1) * R.steps, extra);
+    const int64_t own = (b == 0) ? R.own0 : min(static_cast<int64_t>(R.steps), extra - (b - 1) * R.steps);
+    const int64_t q_off = (b == 0) ? 0 : R.own0 + before;
+    const int64_t k_off = (b == 0) ? 0 : R.own0 + (b - 1) * R.remaining + before;
+    const int64_t seq = (b == 0) ? R.own0 : R.remaining + own;
+    bad = bad || own <= 0 || R.out_base + q_off + own > M.total_prefix ||
+          R.suffix_base + k_off + seq > M.total_suffix || R.beam_base + b + 1 > M.total_beams;
+    if (bad) {
+      if (lane == 0 && M.err) atomicOr(M.err, GR_DEVERR_BAD_RECORD);
+      continue;
+    }
+    const int64_t own_start = R.out_base + R.own0 + (b - 1) * R.steps;   // beam b >= 1: its own tokens
+    for (int64_t j = lane; j < seq; j += 32) {
+      const int64_t val = (b == 0 || j < R.remaining) ? R.out_base + j : own_start + (j - R.remaining);
+      M.smo[R.suffix_base + k_off + j] = static_cast<int32_t>(val);
+    }
+    for (int64_t i = lane; i < own; i += 32) M.prefix_indices[R.out_base + q_off + i] = R.q_start + q_off + i;
+    if (lane == 0) {
+      M.cu_q[R.beam_base + b + 1] = static_cast<int32_t>(R.out_base + q_off + own);
+      M.cu_k[R.beam_base + b + 1] = static_cast<int32_t>(R.suffix_base + k_off + seq);
+    }
+  }
+}
+
 struct Dev {
   int sms = 0;
   int occ_rows = 0;    // resident CTAs per SM of gather_rows_kernel
@@ -240,5 +299,39 @@ extern "C" int32_t gr_suffix_kv_gather(const gr_kv_gather_desc* d, const void* k
   } else {
     gather_elems_kernel<uint8_t><<<grid, kThreads, 0, s>>>(P);
   }
+  return cudaGetLastError() == cudaSuccess ? GR_OK : GR_ERR_CUDA;
+}
+
+extern "C" int32_t gr_suffix_metadata(const gr_suffix_req* reqs, int32_t num_reqs, int64_t total_beams,
+                                      int64_t total_prefix, int64_t total_suffix, int64_t* prefix_indices,
+                                      int32_t* slot_mapping_out, int32_t* cu_seqlens_q, int32_t* cu_seqlens_k,
+                                      int32_t* err, void* stream) {
+  using namespace grkv;
+  if (num_reqs < 0 || total_beams < 0 || total_prefix < 0 || total_suffix < 0) return GR_ERR_BAD_DESC;
+  if (!cu_seqlens_q || !cu_seqlens_k) return GR_ERR_NULL;
+  if ((num_reqs == 0) != (total_beams == 0)) return GR_ERR_BAD_DESC;
+  if (total_beams > 0 && (!reqs || !prefix_indices || !slot_mapping_out)) return GR_ERR_NULL;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GR_ERR_NO_DEVICE;
+  if (g_dev[dev].sms == 0) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return GR_ERR_CUDA;
+    g_dev[dev].sms = sms;
+  }
+  MetaParams M;
+  M.reqs = reqs;
+  M.num_reqs = num_reqs;
+  M.total_beams = total_beams;
+  M.total_prefix = total_prefix;
+  M.total_suffix = total_suffix;
+  M.prefix_indices = prefix_indices;
+  M.smo = slot_mapping_out;
+  M.cu_q = cu_seqlens_q;
+  M.cu_k = cu_seqlens_k;
+  M.err = err;
+  const int64_t want = (total_beams + kWarps - 1) / kWarps;
+  const int64_t cap = static_cast<int64_t>(g_dev[dev].sms) * 4;
+  const int grid = static_cast<int>(want < 1 ? 1 : (want < cap ? want : cap));
+  suffix_metadata_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(M);
   return cudaGetLastError() == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
