@@ -665,6 +665,33 @@ def run_suffix_kv(args):
             "cpu_baseline": {"value": round(cpu_gbs, 2), "unit": "GB/s", "cores": 1, "kind": "port",
                              "sample": f"{ns} tokens (oracle/suffix_kv.py NumPy gather, fp32 copy of the cache)"},
         })
+    # suffix-pass metadata for the shared_tail layout: the device builder
+    # (host records + copy + kernel, synchronised) against the reference
+    # builder's Python loops (oracle/suffix_kv.py restates them)
+    from oracle import suffix_kv as osk
+    from vllm_gr_ehaleva_b200.attention import build_suffix_metadata
+    shared, steps = 24, 8
+    mega = [dict(prefix_len=shared, cache_len=0, beam_width=B, steps=steps)] * R
+    q_starts = list(range(0, (shared + B * steps) * R + 1, shared + B * steps))
+    for _ in range(3):
+        build_suffix_metadata(mega, q_starts, block, device)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(50):
+        m = build_suffix_metadata(mega, q_starts, block, device)
+    torch.cuda.synchronize()
+    dev_ms = (time.perf_counter() - t0) / 50 * 1e3
+    t0 = time.perf_counter()
+    for _ in range(3):
+        ref = osk.suffix_metadata(mega, q_starts, block)
+    py_ms = (time.perf_counter() - t0) / 3 * 1e3
+    same = bool(np.array_equal(m["suffix_slot_mapping_out"].cpu().numpy(), ref[1]))
+    lines.append({"metric": "suffix-pass metadata build time", "layout": "shared_tail", "value": round(dev_ms, 4),
+                  "unit": "ms", "higher_is_better": False, "suffix_tokens": int(m["suffix_total_tokens"]),
+                  "python_builder_ms": round(py_ms, 3), "matches_python_builder": same,
+                  "config": {"requests": R, "beams": B, "shared_tail": shared, "steps": steps},
+                  "note": "device: host records + one copy + gr_suffix_metadata, wall clock with a sync per call; "
+                          "python: the reference builder's loops (oracle/suffix_kv.py), one host core"})
     for line in lines:
         print(json.dumps(line), flush=True)
 
