@@ -56,8 +56,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--requests", type=int, default=None, help="override requests per GPU")
-    ap.add_argument("--component", default="step", choices=["step", "suffix_kv"],
-                    help="suffix_kv: time the suffix KV gather of the attention pass instead of the step")
+    ap.add_argument("--component", default="step", choices=["step", "suffix_kv", "wire"],
+                    help="suffix_kv: the suffix KV gather of the attention pass; wire: the step message (host)")
     return ap.parse_args()
 
 
@@ -696,10 +696,59 @@ def run_suffix_kv(args):
         print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ step message (host)
+def run_wire(args):
+    """Build + encode + decode + the core's token list for one mega-request step
+    message: the int32 form (vllm_gr_ehaleva_b200.wire, from the step's parent
+    indices and fork table) against the reference's per-beam string ids and token
+    lists (restated in oracle/wire_ref.py).  Host only."""
+    import msgspec
+    from oracle import wire_ref
+    from vllm_gr_ehaleva_b200 import wire
+    rng = np.random.default_rng(3)
+    for B, steps in ((128, 3), (512, 4), (1024, 3)):
+        prefix = list(range(100, 164))
+        parents = rng.integers(0, B, B).astype(np.int32)
+        toks = rng.integers(127488, 152064, (B, steps)).astype(np.int32)
+        prev_ids = [f"req-prev0000-beam-{j}" for j in range(B)]
+        beams = [prefix + t for t in toks.tolist()]
+        fork_info = list(zip(parents.tolist(), toks[:, -1].tolist()))
+
+        def ours():
+            f = wire.build_step_fork("sess", "req-next0000", "req-prev0000", B, parents, toks, len(prefix))
+            g = wire.decode(wire.encode(f))
+            return wire.mega_token_ids(g, prefix)
+
+        def ref():
+            u = wire_ref.build("sess", fork_info, prev_ids, beams, "req-next0000", len(prefix))
+            v = msgspec.msgpack.decode(msgspec.msgpack.encode(u), type=wire_ref.RefStepUpdate)
+            return wire_ref.mega_token_ids(v, prefix)
+
+        def t(fn, n=200):
+            fn()
+            t0 = time.perf_counter()
+            for _ in range(n):
+                fn()
+            return (time.perf_counter() - t0) / n * 1e3
+
+        assert np.array_equal(ours(), np.asarray(ref()))
+        f = wire.build_step_fork("sess", "req-next0000", "req-prev0000", B, parents, toks, len(prefix))
+        u = wire_ref.build("sess", fork_info, prev_ids, beams, "req-next0000", len(prefix))
+        print(json.dumps({"metric": "mega-request step message: build + encode + decode + core token list",
+                          "beams": B, "steps": steps, "value": round(t(ours), 4), "unit": "ms",
+                          "higher_is_better": False, "bytes": len(wire.encode(f)),
+                          "reference_format_ms": round(t(ref), 4),
+                          "reference_format_bytes": len(msgspec.msgpack.encode(u)),
+                          "note": "host, one core; SamplingParams excluded from both"}), flush=True)
+
+
 def main():
     args = parse()
     if args.component == "suffix_kv":
         run_suffix_kv(args)
+        return
+    if args.component == "wire":
+        run_wire(args)
         return
     if args.impl == "reference":
         run_reference(args)
