@@ -56,8 +56,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--requests", type=int, default=None, help="override requests per GPU")
-    ap.add_argument("--component", default="step", choices=["step", "suffix_kv", "wire"],
-                    help="suffix_kv: the suffix KV gather of the attention pass; wire: the step message (host)")
+    ap.add_argument("--component", default="step", choices=["step", "suffix_kv", "wire", "remux"],
+                    help="suffix_kv: the suffix KV gather of the attention pass; wire: the step message (host); "
+                         "remux: the worker's logprobs remux")
     return ap.parse_args()
 
 
@@ -742,8 +743,56 @@ def run_wire(args):
                           "note": "host, one core; SamplingParams excluded from both"}), flush=True)
 
 
+# ------------------------------------------------------------------ logprobs remux
+def run_remux(args):
+    """gr_remux_logprobs against per-request torch slices / pads / cat (the
+    reference's way, restated in oracle/remux.py), 64 mega requests x 128 rows
+    x K = 129 (logprobs = beam width, plus the sampled token), CUDA events."""
+    import torch
+    from oracle import remux as orx
+    from vllm_gr_ehaleva_b200.engine import remux_logprobs_tensors
+    dev = torch.device("cuda", 0)
+    ws = [128] * 64
+    K = 129
+    rows = sum(ws)
+    lps = torch.randn(rows, K, device=dev)
+    ids = torch.randint(0, 150000, (rows, K), device=dev, dtype=torch.int32)
+    ranks = torch.randint(1, 99, (rows,), device=dev, dtype=torch.int32)
+    st = torch.randint(0, 150000, (rows, 1), device=dev, dtype=torch.int32)
+    cfg = [(i, 0, w) for i, w in enumerate(ws)]
+    max_dim = max(ws) * K
+
+    def timed(fn, iters=100):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
+
+    ours = timed(lambda: remux_logprobs_tensors(cfg, max_dim, K, lps, ids, ranks, st))
+    ref = timed(lambda: orx.remux_torch(ws, max_dim, K, lps, ids, ranks, st))
+    a = remux_logprobs_tensors(cfg, max_dim, K, lps, ids, ranks, st)
+    b = orx.remux_torch(ws, max_dim, K, lps, ids, ranks, st)
+    same = all(bool(torch.equal(x, y)) for x, y in zip(a, b))
+    moved = rows * K * 8 + rows * 8 + len(ws) * max_dim * 12
+    print(json.dumps({"metric": "logprobs remux per step", "value": round(ours, 4), "unit": "ms",
+                      "higher_is_better": False, "reference_way_ms": round(ref, 4), "exact": same,
+                      "bytes_per_call": moved, "achieved_gbs": round(moved / (ours * 1e-3) / 1e9, 1),
+                      "config": {"requests": len(ws), "rows_per_request": 128, "K": K},
+                      "note": "ours: host offsets + two small copies + one kernel; reference way: torch "
+                              "slices / pads / cat per request (oracle/remux.py)"}), flush=True)
+
+
 def main():
     args = parse()
+    if args.component == "remux":
+        run_remux(args)
+        return
     if args.component == "suffix_kv":
         run_suffix_kv(args)
         return

@@ -290,6 +290,37 @@ int32_t gr_suffix_metadata(const gr_suffix_req* reqs, int32_t num_reqs, int64_t 
                            int32_t* slot_mapping_out, int32_t* cu_seqlens_q, int32_t* cu_seqlens_k,
                            int32_t* err, void* stream);
 
+/* ---- logprobs remux of mega requests (worker side) -----------------------
+ *
+ * vLLM's sampler returns K logprobs (and token ids) per logit row and one
+ * rank per row; a mega request owns `row_w[c]` consecutive rows (0 for a
+ * chunked prefill that produced none).  Per request c this writes one row:
+ *   out_lps[c][j]   = lps[(row_start[c] + j / K) * lps_stride + j % K]   j < row_w*K, else -inf
+ *   out_ids[c][j]   = ids[... same ...]                                   else 0
+ *   out_ranks[c][j] = ranks[row_start[c] + j]                              j < row_w, else 0
+ *   out_st[c]       = st[row_start[c] * st_stride]                         row_w > 0, else -1
+ * for j < max_dim.  Integer arrays are 4- or 8-byte (ids_bytes / ranks_bytes
+ * 0 = the array is absent).  row_w and row_start are device arrays.
+ * Replaces vllm_gr/v1/engine/engine_core_patch.py:383-445
+ * (_remux_logprobs_tensors: a Python loop of slices, pads and one cat). */
+typedef struct gr_remux_desc {
+  int32_t num_requests;
+  int32_t K;                 /* logprob columns taken per row (<= the rows' width) */
+  int64_t max_dim;           /* output row width (>= max row_w * K)                 */
+  int64_t num_rows;          /* sampler rows                                        */
+  int64_t lps_stride;        /* elements between sampler rows of lps / ids          */
+  int64_t ids_stride;
+  int64_t st_stride;         /* elements between rows of st                         */
+  int32_t ids_bytes;         /* 0, 4 or 8                                           */
+  int32_t ranks_bytes;       /* 0, 4 or 8                                           */
+  int32_t st_bytes;          /* 4 or 8                                              */
+  int32_t reserved;
+} gr_remux_desc;
+
+int32_t gr_remux_logprobs(const gr_remux_desc* desc, const int32_t* row_w, const int64_t* row_start,
+                          const float* lps, const void* ids, const void* ranks, const void* st,
+                          float* out_lps, void* out_ids, void* out_ranks, void* out_st, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,7 +17,7 @@ ROOT = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_NAME = "_gr_beam.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
-SOURCES = ["gr_beam_step.cu", "gr_suffix_kv.cu"]
+SOURCES = ["gr_beam_step.cu", "gr_suffix_kv.cu", "gr_remux.cu"]
 HEADERS = ["gr_device.cuh", "gr_step_ws.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
