@@ -92,3 +92,51 @@ def test_sampler_refuses_to_run_without_the_library(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "_lib", None)
     with pytest.raises(ImportError):
         _lib.load(str(tmp_path / "missing.so"))
+
+
+def test_attention_and_worker_struct_layouts_match_header():
+    src = r'''
+#include <stdio.h>
+#include <stddef.h>
+#include "gr_beam.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu %zu %zu %zu\n", sizeof(gr_kv_gather_desc), offsetof(gr_kv_gather_desc, k_stride_tok),
+         sizeof(gr_suffix_req), offsetof(gr_suffix_req, beam_base), offsetof(gr_suffix_req, own_total),
+         sizeof(gr_remux_desc), offsetof(gr_remux_desc, max_dim), offsetof(gr_remux_desc, ids_bytes));
+  return 0;
+}
+'''
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "probe.c")
+        exe = os.path.join(d, "probe")
+        open(c, "w").write(src)
+        subprocess.run(["gcc", "-I", os.path.dirname(HEADER), c, "-o", exe], check=True)
+        got = list(map(int, subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()))
+    want = [ctypes.sizeof(_lib.KvGatherDesc), _lib.KvGatherDesc.k_stride_tok.offset, ctypes.sizeof(_lib.SuffixReq),
+            _lib.SuffixReq.beam_base.offset, _lib.SuffixReq.own_total.offset, ctypes.sizeof(_lib.RemuxDesc),
+            _lib.RemuxDesc.max_dim.offset, _lib.RemuxDesc.ids_bytes.offset]
+    assert got == want
+
+
+def test_attention_and_worker_entry_points_validate_without_a_device():
+    # every case below returns before any CUDA call
+    lib = _lib.load()
+    g = _lib.KvGatherDesc(num_out=0, num_src=1, num_slots=1, num_heads=1, head_dim=8, elem_bytes=2)
+    assert lib.gr_suffix_kv_gather(None, None, None, None, None, None, None, None, None) == -1
+    assert lib.gr_suffix_kv_gather(ctypes.byref(g), None, None, None, None, None, None, None, None) == 0
+    g.elem_bytes = 3
+    assert lib.gr_suffix_kv_gather(ctypes.byref(g), None, None, None, None, None, None, None, None) == -3
+    g.elem_bytes, g.num_heads = 2, 0
+    assert lib.gr_suffix_kv_gather(ctypes.byref(g), None, None, None, None, None, None, None, None) == -2
+    # metadata: sizes negative or records without beams / beams without records
+    assert lib.gr_suffix_metadata(None, 0, 0, 0, -1, None, None, None, None, None, None) == -2
+    out = (ctypes.c_int32 * 2)()
+    assert lib.gr_suffix_metadata(None, 1, 0, 0, 0, None, None, out, out, None, None) == -2
+    assert lib.gr_suffix_metadata(None, 0, 0, 0, 0, None, None, None, None, None, None) == -1
+    # remux: K must be positive, integer widths 0/4/8, st 4/8; no request -> nothing to do
+    r = _lib.RemuxDesc(num_requests=0, K=4, max_dim=8, num_rows=0, st_bytes=4)
+    assert lib.gr_remux_logprobs(ctypes.byref(r), *([None] * 10), None) == 0
+    r.K = 0
+    assert lib.gr_remux_logprobs(ctypes.byref(r), *([None] * 10), None) == -2
+    r.K, r.ids_bytes = 4, 2
+    assert lib.gr_remux_logprobs(ctypes.byref(r), *([None] * 10), None) == -3
