@@ -212,3 +212,24 @@ def test_device_metadata_rejects_inconsistent_records():
     torch.cuda.synchronize()
     assert int(err.item()) & 0x40
     assert (pi == -7).all() and (smo == -7).all()
+
+
+def test_metadata_first_then_gather_in_a_fresh_process():
+    # both entry points share one per-device record: the first call of either must set all of it
+    import subprocess
+    import sys
+    code = r'''
+import torch
+from vllm_gr_ehaleva_b200.attention import build_suffix_metadata, extract_suffix_kv
+m = build_suffix_metadata([dict(prefix_len=3, cache_len=0, beam_width=4, steps=2)], [0, 11], 16, "cuda")
+k = torch.randn(2, 16, 2, 64, device="cuda").to(torch.bfloat16)
+sm = torch.arange(32, device="cuda")
+ok, ov = extract_suffix_kv(k, k, sm, m["suffix_slot_mapping_out"], m["suffix_total_tokens"])
+torch.cuda.synchronize()
+exp = k.view(-1, 2, 64)[sm[m["suffix_slot_mapping_out"].long()]]
+assert torch.equal(ok, exp), "gather after metadata"
+print("ok")
+'''
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]

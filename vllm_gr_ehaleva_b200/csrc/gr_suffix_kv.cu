@@ -26,6 +26,7 @@
 
 #include <cstdint>
 #include <cuda_runtime.h>
+#include <mutex>
 
 #include "../../include/gr_beam.h"
 
@@ -230,6 +231,27 @@ struct Dev {
   int occ_elems = 0;   // of gather_elems_kernel (the 4-byte instance)
 };
 static Dev g_dev[64];
+static std::mutex g_dev_mu;
+
+// The current device's SM count and the kernels' resident CTAs per SM, looked
+// up once per device (every entry point of this file uses the same record).
+static int device_info(Dev& out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GR_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  if (g_dev[dev].sms == 0) {
+    int sms = 0, a = 0, b = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return GR_ERR_CUDA;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, gather_rows_kernel, kThreads, 0) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, gather_elems_kernel<uint32_t>, kThreads, 0) != cudaSuccess)
+      return GR_ERR_CUDA;
+    g_dev[dev].occ_rows = a > 0 ? a : 1;
+    g_dev[dev].occ_elems = b > 0 ? b : 1;
+    g_dev[dev].sms = sms;
+  }
+  out = g_dev[dev];
+  return GR_OK;
+}
 
 }  // namespace grkv
 
@@ -243,18 +265,9 @@ extern "C" int32_t gr_suffix_kv_gather(const gr_kv_gather_desc* d, const void* k
   if (d->elem_bytes != 1 && d->elem_bytes != 2 && d->elem_bytes != 4) return GR_ERR_DTYPE;
   if (d->num_out == 0) return GR_OK;
   if (!k_cache || !v_cache || !slot_mapping || !slot_mapping_out || !out_k || !out_v) return GR_ERR_NULL;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GR_ERR_NO_DEVICE;
-  if (g_dev[dev].sms == 0) {
-    int sms = 0, a = 0, b = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return GR_ERR_CUDA;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, gather_rows_kernel, kThreads, 0) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, gather_elems_kernel<uint32_t>, kThreads, 0) != cudaSuccess)
-      return GR_ERR_CUDA;
-    g_dev[dev].occ_rows = a > 0 ? a : 1;
-    g_dev[dev].occ_elems = b > 0 ? b : 1;
-    g_dev[dev].sms = sms;
-  }
+  Dev info;
+  const int rc = device_info(info);
+  if (rc != GR_OK) return rc;
   Params P;
   P.k = static_cast<const unsigned char*>(k_cache);
   P.v = static_cast<const unsigned char*>(v_cache);
@@ -287,7 +300,7 @@ extern "C" int32_t gr_suffix_kv_gather(const gr_kv_gather_desc* d, const void* k
   // at least ~8 tokens per warp, then every resident CTA
   const int64_t want = (d->num_out + 8 * kWarps - 1) / (8 * kWarps);
   // a persistent grid: every CTA resident at once
-  const int64_t cap = static_cast<int64_t>(g_dev[dev].sms) * (vec ? g_dev[dev].occ_rows : g_dev[dev].occ_elems);
+  const int64_t cap = static_cast<int64_t>(info.sms) * (vec ? info.occ_rows : info.occ_elems);
   const int grid = static_cast<int>(want < cap ? want : cap);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (vec) {
@@ -311,13 +324,9 @@ extern "C" int32_t gr_suffix_metadata(const gr_suffix_req* reqs, int32_t num_req
   if (!cu_seqlens_q || !cu_seqlens_k) return GR_ERR_NULL;
   if ((num_reqs == 0) != (total_beams == 0)) return GR_ERR_BAD_DESC;
   if (total_beams > 0 && (!reqs || !prefix_indices || !slot_mapping_out)) return GR_ERR_NULL;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GR_ERR_NO_DEVICE;
-  if (g_dev[dev].sms == 0) {
-    int sms = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return GR_ERR_CUDA;
-    g_dev[dev].sms = sms;
-  }
+  Dev info;
+  const int rc = device_info(info);
+  if (rc != GR_OK) return rc;
   MetaParams M;
   M.reqs = reqs;
   M.num_reqs = num_reqs;
@@ -330,7 +339,7 @@ extern "C" int32_t gr_suffix_metadata(const gr_suffix_req* reqs, int32_t num_req
   M.cu_k = cu_seqlens_k;
   M.err = err;
   const int64_t want = (total_beams + kWarps - 1) / kWarps;
-  const int64_t cap = static_cast<int64_t>(g_dev[dev].sms) * 4;
+  const int64_t cap = static_cast<int64_t>(info.sms) * 4;
   const int grid = static_cast<int>(want < 1 ? 1 : (want < cap ? want : cap));
   suffix_metadata_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(M);
   return cudaGetLastError() == cudaSuccess ? GR_OK : GR_ERR_CUDA;
