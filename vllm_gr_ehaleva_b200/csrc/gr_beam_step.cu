@@ -2134,11 +2134,15 @@ struct DeviceInfo {
 };
 
 static DeviceInfo g_dev[64];
+// Guards the per-device records (filled on a device's first call) and their
+// kernel-attribute flags: calls may come from several host threads.
+static std::mutex g_dev_mu;
 
 static int device_info(DeviceInfo** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return GR_ERR_NO_DEVICE;
   if (dev < 0 || dev >= 64) return GR_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_dev_mu);
   DeviceInfo& d = g_dev[dev];
   if (d.sms == 0) {
     int sms = 0, smem = 0, major = 0;
@@ -2280,12 +2284,14 @@ static int launch_fused(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream_t 
   if (stages == 0) return GR_ERR_UNSUPPORTED;
   P.stages = stages;
   const size_t smem = smem_bytes(stages, P.win_bytes, P.bm_words, P.tab_cap, P.pen);
+  std::unique_lock<std::mutex> attr_lock(g_dev_mu);
   if (!dev->attr_set[dtype_idx]) {
     if (cudaFuncSetAttribute(fused_step_kernel<TL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              dev->smem_optin) != cudaSuccess)
       return GR_ERR_CUDA;
     dev->attr_set[dtype_idx] = true;
   }
+  attr_lock.unlock();
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fused_step_kernel<TL>, kBlock, smem) != cudaSuccess)
     return GR_ERR_CUDA;
@@ -2343,12 +2349,14 @@ static int launch_fused_ws(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream
   if (stages == 0) return launch_fused<TL>(P, dev, dtype_idx, stream);
   P.stages = stages;
   const size_t smem = ws::smem_bytes(stages);
+  std::unique_lock<std::mutex> attr_lock(g_dev_mu);
   if (!dev->ws_attr_set[dtype_idx]) {
     if (cudaFuncSetAttribute(fused_step_ws_kernel<TL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              dev->smem_optin) != cudaSuccess)
       return GR_ERR_CUDA;
     dev->ws_attr_set[dtype_idx] = true;
   }
+  attr_lock.unlock();
   const int total = P.R * P.NB;
   const int grid = total < dev->sms ? total : dev->sms;
   if (launch_pdl(fused_step_ws_kernel<TL>, dim3(grid), dim3(ws::kBlockWs), smem, stream, P) != cudaSuccess)
