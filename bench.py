@@ -56,9 +56,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--requests", type=int, default=None, help="override requests per GPU")
-    ap.add_argument("--component", default="step", choices=["step", "suffix_kv", "wire", "remux"],
+    ap.add_argument("--component", default="step", choices=["step", "suffix_kv", "wire", "remux", "hook"],
                     help="suffix_kv: the suffix KV gather of the attention pass; wire: the step message (host); "
-                         "remux: the worker's logprobs remux")
+                         "remux: the worker's logprobs remux; hook: the worker-side step over cfg2 sessions")
     return ap.parse_args()
 
 
@@ -788,8 +788,70 @@ def run_remux(args):
                               "slices / pads / cat per request (oracle/remux.py)"}), flush=True)
 
 
+# ------------------------------------------------------------------ worker-side step
+def run_hook(args):
+    """cfg2's root level through WorkerBeamHook (32 sessions of 128 beams in the
+    worker's row layout, the same state every call) against one direct step
+    call over the same rows."""
+    import torch
+    from vllm_gr_ehaleva_b200.engine import WorkerBeamHook
+    from vllm_gr_ehaleva_b200.sample import beam_step
+    from vllm_gr_ehaleva_b200.sample.beam_search_sampler import Workspace
+    dev = torch.device("cuda", 0)
+    wl = build_workload("cfg2", None, dev)
+    R, B, V = wl["R"], wl["B"], wl["V"]
+    cat = wl["catalog"]
+    cum0 = torch.from_numpy(initial_cum(R, B)).to(dev)
+    node0 = torch.full((R, B), cat.start_node, dtype=torch.int32, device=dev)
+    logits = wl["logits"][0]
+    cfg = []
+    for r in range(R):
+        cfg.append((f"s{r}", r, B))
+    hook = WorkerBeamHook(vocab_size=V, csr=wl["csr_dev"], device=dev)
+    ws = Workspace(dev)
+
+    for r in range(R):
+        hook.start(f"s{r}", B, cum0[r], node0[r])
+    first = {"ids": tuple(f"s{r}" for r in range(R)), "cum": cum0, "node": node0,
+             "hist": torch.zeros((R, B, 0), dtype=torch.int32, device=dev)}
+
+    def via_hook():
+        # every iteration steps the same root-level state (the sessions point back at it)
+        for r in range(R):
+            s = hook.sessions[f"s{r}"]
+            s._batch, s._idx = first, r
+        return hook.step(logits, cfg)
+
+    def direct():
+        return beam_step(logits, cum0, node0, beam_width=B, csr=wl["csr_dev"], vocab_size=V, workspace=ws)
+
+    def timed(fn, iters=50):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
+
+    h = timed(via_hook)
+    d = timed(direct)
+    a, b = via_hook(), direct()
+    same = all(bool(torch.equal(a[f"s{r}"].sel_token, b.sel_token[r])) for r in range(R))
+    print(json.dumps({"metric": "worker-side step (root level of cfg2, 32 sessions x 128 beams)", "unit": "ms",
+                      "value": round(h, 4), "higher_is_better": False, "direct_step_ms": round(d, 4),
+                      "same_beams": same, "note": "hook: run grouping + one step call on the rows + the "
+                                                  "sessions' state update; direct: one step call"}), flush=True)
+
+
 def main():
     args = parse()
+    if args.component == "hook":
+        run_hook(args)
+        return
     if args.component == "remux":
         run_remux(args)
         return

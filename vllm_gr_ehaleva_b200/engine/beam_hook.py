@@ -20,7 +20,6 @@ and take one step call on a view of their rows (no copy of the logits).
 """
 from __future__ import annotations
 
-from dataclasses import dataclass
 from typing import Optional
 
 import torch
@@ -28,22 +27,47 @@ import torch
 from ..sample.beam_search_sampler import Workspace, beam_step
 
 
-@dataclass
 class SessionState:
-    beam_width: int
-    cum: torch.Tensor     # float32 [B]
-    node: torch.Tensor    # int32 [B]
-    hist: torch.Tensor    # int32 [B, T] tokens since the prompt (the fork table)
+    """A session's beams.  After a step the state points into that step's
+    batched outputs (row `idx` of the run's tensors), so that a run of the same
+    sessions in the same order feeds the next step without copies."""
+    __slots__ = ("beam_width", "_own", "_batch", "_idx")
+
+    def __init__(self, beam_width, cum, node, hist):
+        self.beam_width = beam_width
+        self._own = (cum, node, hist)
+        self._batch = None
+        self._idx = 0
+
+    @property
+    def cum(self):      # float32 [B]
+        return self._own[0] if self._batch is None else self._batch["cum"][self._idx]
+
+    @property
+    def node(self):     # int32 [B]
+        return self._own[1] if self._batch is None else self._batch["node"][self._idx]
+
+    @property
+    def hist(self):     # int32 [B, T]: tokens since the prompt (the fork table)
+        return self._own[2] if self._batch is None else self._batch["hist"][self._idx]
+
+    def hist_len(self) -> int:
+        return self._own[2].shape[1] if self._batch is None else self._batch["hist"].shape[2]
 
 
-@dataclass
 class SessionStep:
-    sel_parent: torch.Tensor   # int32 [B]
-    sel_token: torch.Tensor    # int32 [B]
-    sel_score: torch.Tensor    # float32 [B]
-    sel_node: torch.Tensor     # int32 [B]
-    hist: torch.Tensor         # int32 [B, T+1]
-    eos_score: torch.Tensor    # float32 [B] per parent beam (NaN: no EOS candidate)
+    """One session's new beams: row `i` of its run's step outputs (read lazily)."""
+    __slots__ = ("_res", "_i")
+
+    def __init__(self, res, i):
+        self._res, self._i = res, i
+
+    sel_parent = property(lambda self: self._res.sel_parent[self._i])   # int32 [B]
+    sel_token = property(lambda self: self._res.sel_token[self._i])     # int32 [B]
+    sel_score = property(lambda self: self._res.sel_score[self._i])     # float32 [B]
+    sel_node = property(lambda self: self._res.sel_node[self._i])       # int32 [B]
+    hist = property(lambda self: self._res.hist_out[self._i])           # int32 [B, T+1]
+    eos_score = property(lambda self: self._res.eos_score[self._i])     # float32 [B] per parent (NaN: none)
 
 
 def step_runs(request_row_configs, sessions) -> list:
@@ -103,24 +127,27 @@ class WorkerBeamHook:
         out = {}
         for first, ids, B in step_runs(request_row_configs, self.sessions):
             states = [self.sessions[r] for r in ids]
-            T = states[0].hist.shape[1]
-            if any(s.hist.shape[1] != T for s in states):
-                # token tables of different lengths: one call per session
-                groups = [([r], first + i * B) for i, r in enumerate(ids)]
+            T = states[0].hist_len()
+            if any(s.hist_len() != T for s in states):
+                groups = [([r], first + i * B) for i, r in enumerate(ids)]   # unequal token tables
             else:
                 groups = [(ids, first)]
             for gids, row0 in groups:
                 st = [self.sessions[r] for r in gids]
-                n = len(gids)
-                res = beam_step(logits[row0:row0 + n * B], torch.stack([s.cum for s in st]),
-                                torch.stack([s.node for s in st]), beam_width=B, csr=self.csr,
+                batch = st[0]._batch
+                if batch is not None and batch["ids"] == tuple(gids) and all(s._batch is batch for s in st):
+                    cum, node, hist = batch["cum"], batch["node"], batch["hist"]   # last step's outputs as they are
+                else:
+                    cum = torch.stack([s.cum for s in st])
+                    node = torch.stack([s.node for s in st])
+                    hist = torch.stack([s.hist for s in st]) if T else None
+                res = beam_step(logits[row0:row0 + len(gids) * B], cum, node, beam_width=B, csr=self.csr,
                                 vocab_size=self.vocab_size, logprobs_mode=self.logprobs_mode,
-                                eos_token_id=self.eos_token_id,
-                                hist=torch.stack([s.hist for s in st]) if T else None,
+                                eos_token_id=self.eos_token_id, hist=hist if T else None,
                                 workspace=self.workspace)
+                new = {"ids": tuple(gids), "cum": res.sel_score, "node": res.sel_node, "hist": res.hist_out}
                 for i, r in enumerate(gids):
                     s = self.sessions[r]
-                    s.cum, s.node, s.hist = res.sel_score[i], res.sel_node[i], res.hist_out[i]
-                    out[r] = SessionStep(res.sel_parent[i], res.sel_token[i], res.sel_score[i], res.sel_node[i],
-                                         res.hist_out[i], res.eos_score[i])
+                    s._batch, s._idx = new, i
+                    out[r] = SessionStep(res, i)
         return out
