@@ -2,7 +2,7 @@
 
 This fills the slot the reference reserves for its beam-search sampler
 (vllm_gr/sample/__init__.py:1-3, planned as sample/beam_search_sampler.py in
-its docs/DESIGN.md "3.6 Sample").  One ``BeamSearchSampler.step`` call takes
+the reference's own design notes, section 3.6 "Sample").  One ``BeamSearchSampler.step`` call takes
 the logits rows of all beams of all requests and returns what the reference's
 per-step host code computes from vLLM's flat logprobs
 (serving_engine.py:457-597 / llm.py:201-280):
