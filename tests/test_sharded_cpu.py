@@ -94,3 +94,53 @@ def test_sharded_orchestration_two_gloo_ranks():
         assert all(v != v for i, row in enumerate(res["eos"]) for j, v in enumerate(row) if (i, j) != (0, 1))
         # this rank's three calls' error words, OR-ed
         assert res["err"] == (1 << r) | (1 << (2 + r)) | (1 << (4 + r))
+
+
+def _dropout_worker(rank, world, port, result_q):
+    # rank 1 leaves before the step; rank 0's first all-gather must fail, not hang
+    import datetime
+    import time
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+        if rank == 1:
+            result_q.put((rank, {"left": True}))
+            result_q.close()
+            result_q.join_thread()                # the message is out before the process is
+            os._exit(0)                           # no barrier, no destroy: a rank that drops out
+        from vllm_gr_ehaleva_b200 import sharded as SH
+
+        def fake_partials(local, cum, node, **kw):
+            t = torch.zeros((R * NB, 2))
+            t.err = torch.zeros(1, dtype=torch.int32)
+            return t
+
+        SH.lse_partials = fake_partials
+        t0 = time.monotonic()
+        try:
+            SH.sharded_beam_step(torch.zeros(R * NB, 10), torch.zeros(R, NB), torch.zeros(R, NB, dtype=torch.int32),
+                                 all_gather=SH.torch_all_gather(), beam_width=B, vocab_size=20, vocab_offset=0,
+                                 eos_token_id=13)
+            result_q.put((rank, {"raised": False}))
+        except Exception as e:                    # the collective's error surfaces to the caller
+            result_q.put((rank, {"raised": True, "kind": type(e).__name__, "secs": time.monotonic() - t0}))
+    except Exception as e:
+        result_q.put((rank, {"error": repr(e)}))
+
+
+def test_rank_dropout_surfaces_as_an_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dropout_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert results[1] == {"left": True}
+    assert "error" not in results[0], results[0]
+    assert results[0]["raised"] and results[0]["secs"] < 60, results[0]
