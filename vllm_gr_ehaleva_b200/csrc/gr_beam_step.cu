@@ -36,6 +36,7 @@
 #include <utility>
 
 #include "../../include/gr_beam.h"
+#include "gr_nvtx.h"
 #include "gr_device.cuh"
 
 namespace gr {
@@ -2494,6 +2495,7 @@ int32_t gr_beam_step_workspace_size(const gr_step_desc* d, size_t* bytes) {
 
 int32_t gr_beam_step(const gr_step_desc* d, const gr_step_io* io, void* workspace, size_t workspace_bytes,
                      void* stream) {
+  gr::NvtxRange nvtx_range("gr_beam_step");
   Params P;
   DeviceInfo* dev = nullptr;
   float* lse_ws = nullptr;
@@ -2533,6 +2535,7 @@ static std::mutex g_noalloc_mu;
 extern "C" {
 
 int32_t gr_beam_step_noalloc(const gr_step_desc* d, const gr_step_io* io, void* stream) {
+  gr::NvtxRange nvtx_range("gr_beam_step_noalloc");
   if (!d || !io) return GR_ERR_NULL;
   size_t need = 0;
   const int v = gr_beam_step_workspace_size(d, &need);
@@ -2558,6 +2561,7 @@ int32_t gr_beam_step_noalloc(const gr_step_desc* d, const gr_step_io* io, void* 
 
 int32_t gr_lse_partials(const gr_step_desc* d, const gr_step_io* io, float* partials, void* workspace,
                         size_t workspace_bytes, void* stream) {
+  gr::NvtxRange nvtx_range("gr_lse_partials");
   if (!partials) return GR_ERR_NULL;
   Params P;
   DeviceInfo* dev = nullptr;
@@ -2575,6 +2579,7 @@ int32_t gr_lse_partials(const gr_step_desc* d, const gr_step_io* io, float* part
 int32_t gr_shard_candidates(const gr_step_desc* d, const gr_step_io* io, const float* gathered_partials,
                             int32_t num_shards, uint64_t* shard_keys, void* workspace, size_t workspace_bytes,
                             void* stream) {
+  gr::NvtxRange nvtx_range("gr_shard_candidates");
   if (!gathered_partials || !shard_keys) return GR_ERR_NULL;
   if (num_shards < 1) return GR_ERR_BAD_DESC;
   if (d && d->per_beam_k != 0) return GR_ERR_UNSUPPORTED;
@@ -2598,6 +2603,7 @@ int32_t gr_shard_candidates(const gr_step_desc* d, const gr_step_io* io, const f
 
 int32_t gr_merge_candidates(const gr_step_desc* d, const gr_step_io* io, const uint64_t* gathered_keys,
                             int32_t num_shards, void* workspace, size_t workspace_bytes, void* stream) {
+  gr::NvtxRange nvtx_range("gr_merge_candidates");
   if (!gathered_keys) return GR_ERR_NULL;
   if (num_shards < 1 || num_shards > 65535) return GR_ERR_BAD_DESC;
   if (d && d->per_beam_k != 0) return GR_ERR_UNSUPPORTED;

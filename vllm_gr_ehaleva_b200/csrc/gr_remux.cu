@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 
 #include "../../include/gr_beam.h"
+#include "gr_nvtx.h"
 
 namespace grrx {
 
@@ -71,6 +72,7 @@ __global__ void __launch_bounds__(kThreads) remux_kernel(const Params P) {
 extern "C" int32_t gr_remux_logprobs(const gr_remux_desc* d, const int32_t* row_w, const int64_t* row_start,
                                      const float* lps, const void* ids, const void* ranks, const void* st,
                                      float* out_lps, void* out_ids, void* out_ranks, void* out_st, void* stream) {
+  gr::NvtxRange nvtx_range("gr_remux_logprobs");
   using namespace grrx;
   if (!d) return GR_ERR_NULL;
   if (d->num_requests < 0 || d->K <= 0 || d->max_dim < 0 || d->num_rows < 0) return GR_ERR_BAD_DESC;

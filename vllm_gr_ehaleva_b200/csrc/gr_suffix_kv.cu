@@ -29,6 +29,7 @@
 #include <mutex>
 
 #include "../../include/gr_beam.h"
+#include "gr_nvtx.h"
 
 namespace grkv {
 
@@ -258,6 +259,7 @@ static int device_info(Dev& out) {
 extern "C" int32_t gr_suffix_kv_gather(const gr_kv_gather_desc* d, const void* k_cache, const void* v_cache,
                                        const int64_t* slot_mapping, const int32_t* slot_mapping_out, void* out_k,
                                        void* out_v, int32_t* err, void* stream) {
+  gr::NvtxRange nvtx_range("gr_suffix_kv_gather");
   using namespace grkv;
   if (!d) return GR_ERR_NULL;
   if (d->num_out < 0 || d->num_src < 0 || d->num_slots < 0 || d->num_heads <= 0 || d->head_dim <= 0)
@@ -319,6 +321,7 @@ extern "C" int32_t gr_suffix_metadata(const gr_suffix_req* reqs, int32_t num_req
                                       int64_t total_prefix, int64_t total_suffix, int64_t* prefix_indices,
                                       int32_t* slot_mapping_out, int32_t* cu_seqlens_q, int32_t* cu_seqlens_k,
                                       int32_t* err, void* stream) {
+  gr::NvtxRange nvtx_range("gr_suffix_metadata");
   using namespace grkv;
   if (num_reqs < 0 || total_beams < 0 || total_prefix < 0 || total_suffix < 0) return GR_ERR_BAD_DESC;
   if (!cu_seqlens_q || !cu_seqlens_k) return GR_ERR_NULL;
