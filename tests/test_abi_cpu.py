@@ -140,3 +140,32 @@ def test_attention_and_worker_entry_points_validate_without_a_device():
     assert lib.gr_remux_logprobs(ctypes.byref(r), *([None] * 10), None) == -2
     r.K, r.ids_bytes = 4, 2
     assert lib.gr_remux_logprobs(ctypes.byref(r), *([None] * 10), None) == -3
+
+
+def test_a_c_program_links_against_the_library():
+    # what a C or C++ caller does: include the header, link the shared library, call it
+    src = r'''
+#include <stdio.h>
+#include "gr_beam.h"
+int main(void) {
+  gr_step_desc d = {0};
+  d.num_requests = 2; d.num_beams = 4; d.beam_width = 4; d.vocab_size = 1000; d.vocab_local = 1000;
+  d.row_stride = 1000; d.logit_dtype = GR_DTYPE_BF16; d.logprobs_mode = GR_LOGPROBS_RAW; d.eos_token_id = -1;
+  size_t n = 0;
+  int st = gr_beam_step_workspace_size(&d, &n);
+  d.beam_width = 0;
+  int bad = gr_beam_step_workspace_size(&d, &n);
+  printf("%d %d %s %d\n", st, bad, gr_status_string(bad), gr_abi_version());
+  return (st == GR_OK && n > 0 && bad == GR_ERR_BAD_DESC) ? 0 : 1;
+}
+'''
+    lib = _lib.LIB_PATH
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "caller.c")
+        exe = os.path.join(d, "caller")
+        open(c, "w").write(src)
+        subprocess.run(["gcc", "-I", os.path.dirname(HEADER), c, lib, f"-Wl,-rpath,{os.path.dirname(lib)}",
+                        "-o", exe], check=True)
+        r = subprocess.run([exe], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert r.stdout.split() == ["0", "-2", "GR_ERR_BAD_DESC", "1"]
