@@ -1158,6 +1158,14 @@ struct FastSum<float> {
 
 // Producer warp, lane 0: fill the ring (stages of SB bytes at `ring`) with the
 // CTA's (row, chunk) sequence.
+// Vocab-sharded phase 2 (the rows' lse given): only rows without a node need
+// their stream (their candidates are streamed values); the others read their
+// child window directly.  Producer and consumers decide it from the same
+// node, so they agree on every row's stage count.
+__device__ __forceinline__ bool stream_skipped(const Params& P, int node) {
+  return P.lse_in != nullptr && P.K == 0 && node != GR_NODE_UNCONSTRAINED;
+}
+
 template <int ES, int SB = kStageBytes>
 __device__ __forceinline__ void produce(const Params& P, int my_n, unsigned char* ring) {
   const Smem S = smem_view(P);
@@ -1166,8 +1174,10 @@ __device__ __forceinline__ void produce(const Params& P, int my_n, unsigned char
   uint32_t round = 0;
   long long fills = 0;
   for (int it = 0; it < my_n; ++it) {
-    const Geom g = row_geom<ES, SB>(P, row_of_iter(P, it));
-    for (int ch = 0; ch < g.nchunks; ++ch) {
+    const int row = row_of_iter(P, it);
+    const Geom g = row_geom<ES, SB>(P, row);
+    const int nch = stream_skipped(P, __ldg(P.meta + static_cast<size_t>(row) * kMetaWords + kMNode)) ? 0 : g.nchunks;
+    for (int ch = 0; ch < nch; ++ch) {
       if (fills >= P.stages) {
         if (!mbar_wait_bounded(&S.empty[stage], (round - 1u) & 1u, &S.v->abort)) {
           if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
@@ -1369,6 +1379,14 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
         st.template process<1>(c, x, tl, valid, m, s, thr_y, thr_key);
       }
     }
+    // vocab-sharded phase 2: no stream for rows with a node; their window's
+    // body columns are read here (the head and tail columns came just above)
+    const int nch = stream_skipped(P, c.node) ? 0 : g.nchunks;
+    if (nch == 0 && g.nchunks > 0 && c.constrained) {
+      const int lo = max(c.wlo, g.head), hi = min(c.whi, g.tail_start - 1);
+      for (int tl = lo + tid; tl <= hi; tl += kThreads) st.win_store(tl - c.wlo, st.load_logit(c, tl));
+      csync();
+    }
     // list length after the last complete append round, and the CTA's lse
     // bound (bounded rows)
     uint32_t cnt_prev = 0;
@@ -1396,7 +1414,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
     // ------------------------------------------------------------ body chunks
     GR_PROF_ADD(5, t_row);
     GR_PROF_T(t_stream);
-    for (int ch = 0; ch < g.nchunks; ++ch) {
+    for (int ch = 0; ch < nch; ++ch) {
       GR_PROF_T(t_wait);
       if (!mbar_wait_bounded(&S.full[cstage], cphase, &S.v->abort)) {
         if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
@@ -2368,7 +2386,10 @@ static int launch_fused_ws(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream
 template <typename TL>
 static int launch_step_kernel(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream_t stream) {
   const int choice = kernel_choice();
-  if (choice != 1 && ws_eligible(P)) return launch_fused_ws<TL>(P, dev, dtype_idx, stream);
+  // a given lse (vocab-sharded phase 2) leaves only row-end work: the streaming
+  // kernel puts every consumer warp on it (GR_BEAM_KERNEL=ws keeps the other)
+  const bool ws = ws_eligible(P) && (P.lse_in == nullptr ? choice != 1 : choice == 2);
+  if (ws) return launch_fused_ws<TL>(P, dev, dtype_idx, stream);
   return launch_fused<TL>(P, dev, dtype_idx, stream);
 }
 
