@@ -280,6 +280,19 @@ typedef struct gr_suffix_req {
   int32_t own_total;     /* all query tokens of the request's mega part            */
 } gr_suffix_req;
 
+/* Host helper (no device, no allocation): the records of gr_suffix_metadata
+ * from the reference builder's per-request inputs, all host arrays of length
+ * num_reqs (mega[i] = 0 marks a standard request; q_starts has num_reqs + 1
+ * entries).  Writes at most num_reqs records to `recs` and the totals
+ * (records, beams, prefix tokens, suffix tokens, max query / suffix length of
+ * a beam) to totals[6].  Follows beam_attn.py:255-292 (a long uncached prefix
+ * first goes through standard attention) and 319-413 (beam 0's share, then
+ * `steps` per beam until the query budget runs out).  GR_ERR_BAD_DESC when a
+ * request's cache_len exceeds its prefix_len after that split. */
+int32_t gr_suffix_records(int32_t num_reqs, const int64_t* q_starts, const uint8_t* mega,
+                          const int32_t* prefix_len, const int32_t* cache_len, const int32_t* beam_width,
+                          const int32_t* steps, int32_t block_size, gr_suffix_req* recs, int64_t* totals);
+
 #define GR_DEVERR_BAD_RECORD    0x40  /* suffix metadata: a record points outside the outputs */
 
 /* prefix_indices has total_prefix entries, slot_mapping_out total_suffix, the

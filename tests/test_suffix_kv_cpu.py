@@ -141,3 +141,45 @@ def test_records_mixed_requests_match_oracle():
         np.testing.assert_array_equal(np.diff(e_cq), q_l)
         np.testing.assert_array_equal(np.diff(e_ck), seq_l)
         assert tot["max_q"] == (max(q_l) if len(q_l) else 0) and tot["max_k"] == (max(seq_l) if len(seq_l) else 0)
+
+
+def _c_records(mega, q_starts, block):
+    """gr_suffix_records through ctypes (host only)."""
+    import ctypes
+    from vllm_gr_ehaleva_b200 import _lib
+    lib = _lib.load()
+    n = len(q_starts) - 1
+    flags = np.array([1 if m else 0 for m in mega], np.uint8)
+    get = lambda k: np.array([int(m[k]) if m else 0 for m in mega], np.int32)  # noqa: E731
+    arrs = [np.asarray(q_starts, np.int64), flags, get("prefix_len"), get("cache_len"), get("beam_width"),
+            get("steps")]
+    recs = (_lib.SuffixReq * max(n, 1))()
+    totals = np.zeros(6, np.int64)
+    rc = lib.gr_suffix_records(n, *[a.ctypes.data for a in arrs], block, ctypes.addressof(recs), totals.ctypes.data)
+    assert rc == 0
+    out = [(r.q_start, r.out_base, r.suffix_base, r.beam_base, r.beams, r.remaining, r.steps, r.own0, r.own_total)
+           for r in recs[:int(totals[0])]]
+    return out, dict(beams=int(totals[1]), prefix=int(totals[2]), suffix=int(totals[3]), max_q=int(totals[4]),
+                     max_k=int(totals[5]))
+
+
+def test_c_records_equal_python_records():
+    from vllm_gr_ehaleva_b200.attention import suffix_records
+    rng = np.random.default_rng(8)
+    for _ in range(60):
+        n = int(rng.integers(0, 9))
+        q_starts = [0] + np.cumsum(rng.integers(0, 300, n)).tolist()
+        mega = []
+        for _i in range(n):
+            if rng.random() < 0.25:
+                mega.append(None)
+                continue
+            p = int(rng.integers(0, 90))
+            mega.append(dict(prefix_len=p, cache_len=int(rng.integers(0, p + 1)), beam_width=int(rng.integers(0, 17)),
+                             steps=int(rng.integers(0, 7))))
+        block = int(rng.choice([16, 32]))
+        assert _c_records(mega, q_starts, block) == suffix_records(mega, q_starts, block)
+    for c in _cases():
+        mega = [dict(prefix_len=c["prefix_len"], cache_len=0, beam_width=c["beam_width"],
+                     steps=c["suffix_kv_len"])] * c["batch_size"]
+        assert _c_records(mega, _q_starts(c), c["block_size"]) == suffix_records(mega, _q_starts(c), c["block_size"])

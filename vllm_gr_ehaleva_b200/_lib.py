@@ -28,7 +28,7 @@ NODE_UNCONSTRAINED, NODE_DEAD = -1, -2
 EXPORTED_SYMBOLS = (
     "gr_abi_version", "gr_status_string", "gr_beam_step_workspace_size", "gr_beam_step",
     "gr_lse_partials", "gr_shard_candidates", "gr_merge_candidates", "gr_beam_step_noalloc",
-    "gr_suffix_kv_gather", "gr_suffix_metadata", "gr_remux_logprobs",
+    "gr_suffix_kv_gather", "gr_suffix_metadata", "gr_suffix_records", "gr_remux_logprobs",
 )
 NOALLOC_SCRATCH_BYTES = 16 << 20
 
@@ -156,6 +156,9 @@ def load(path: str | None = None) -> ctypes.CDLL:
     lib.gr_suffix_metadata.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
                                        ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    lib.gr_suffix_records.restype = ctypes.c_int32
+    lib.gr_suffix_records.argtypes = [ctypes.c_int32] + [ctypes.c_void_p] * 6 + [ctypes.c_int32, ctypes.c_void_p,
+                                                                                ctypes.c_void_p]
     lib.gr_remux_logprobs.restype = ctypes.c_int32
     lib.gr_remux_logprobs.argtypes = [P(RemuxDesc)] + [ctypes.c_void_p] * 11
     _lib = lib

@@ -347,3 +347,60 @@ extern "C" int32_t gr_suffix_metadata(const gr_suffix_req* reqs, int32_t num_req
   suffix_metadata_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(M);
   return cudaGetLastError() == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
+
+extern "C" int32_t gr_suffix_records(int32_t num_reqs, const int64_t* q_starts, const uint8_t* mega,
+                                     const int32_t* prefix_len, const int32_t* cache_len,
+                                     const int32_t* beam_width, const int32_t* steps, int32_t block_size,
+                                     gr_suffix_req* recs, int64_t* totals) {
+  if (num_reqs < 0 || block_size <= 0) return GR_ERR_BAD_DESC;
+  if (!totals) return GR_ERR_NULL;
+  if (num_reqs > 0 && (!q_starts || !mega || !prefix_len || !cache_len || !beam_width || !steps || !recs))
+    return GR_ERR_NULL;
+  int64_t n = 0, out_base = 0, suffix_base = 0, beam_base = 0, max_q = 0, max_k = 0;
+  for (int32_t i = 0; i < num_reqs; ++i) {
+    if (!mega[i]) continue;
+    const int64_t plen = prefix_len[i], w = beam_width[i], st = steps[i];
+    int64_t clen = cache_len[i], q_offset = 0;
+    const int64_t delta = plen - clen;
+    if (delta > 0 && delta >= 2 * static_cast<int64_t>(block_size)) {
+      // a long uncached prefix runs through standard attention first
+      const int64_t std_q = delta < q_starts[i + 1] - q_starts[i] ? delta : q_starts[i + 1] - q_starts[i];
+      clen += std_q;
+      q_offset = std_q;
+    }
+    const int64_t q_start = q_starts[i] + q_offset;
+    const int64_t q_len = q_starts[i + 1] - q_start;
+    if (w == 0 || st == 0 || q_len <= 0) continue;
+    const int64_t remaining = plen - clen;
+    if (remaining < 0 || w < 0 || st < 0) return GR_ERR_BAD_DESC;
+    const int64_t own0 = q_len < remaining + st ? q_len : remaining + st;
+    const int64_t room = q_len - own0, full = (w - 1) * st;
+    const int64_t extra = room < full ? room : full;
+    const int64_t beams = 1 + (extra + st - 1) / st;
+    gr_suffix_req& r = recs[n++];
+    r.q_start = q_start;
+    r.out_base = out_base;
+    r.suffix_base = suffix_base;
+    r.beam_base = static_cast<int32_t>(beam_base);
+    r.beams = static_cast<int32_t>(beams);
+    r.remaining = static_cast<int32_t>(remaining);
+    r.steps = static_cast<int32_t>(st);
+    r.own0 = static_cast<int32_t>(own0);
+    r.own_total = static_cast<int32_t>(own0 + extra);
+    const int64_t q1 = extra < st ? extra : st;
+    if (own0 > max_q) max_q = own0;
+    if (q1 > max_q) max_q = q1;
+    if (own0 > max_k) max_k = own0;
+    if (extra > 0 && remaining + q1 > max_k) max_k = remaining + q1;
+    out_base += own0 + extra;
+    suffix_base += own0 + (beams - 1) * remaining + extra;
+    beam_base += beams;
+  }
+  totals[0] = n;
+  totals[1] = beam_base;
+  totals[2] = out_base;
+  totals[3] = suffix_base;
+  totals[4] = max_q;
+  totals[5] = max_k;
+  return GR_OK;
+}
