@@ -71,7 +71,9 @@ typedef enum gr_status {
 #define GR_DEVERR_BAD_CHILD     0x2   /* CSR child token outside [0, vocab)     */
 #define GR_DEVERR_TIMEOUT       0x4   /* a bounded mbarrier wait ran out        */
 #define GR_DEVERR_OVERFLOW      0x8   /* per-request candidate buffer overflow  */
-#define GR_DEVERR_TIE_BOUNDARY  0x10  /* streamed top-k boundary not exact      */
+#define GR_DEVERR_TIE_BOUNDARY  0x10  /* reserved: no longer raised (a streamed
+                                         top-k whose boundary could tie a dropped
+                                         column is recomputed exactly)          */
 
 typedef enum gr_dtype {
   GR_DTYPE_F32 = 0,
@@ -197,7 +199,9 @@ int32_t gr_lse_partials(const gr_step_desc* desc, const gr_step_io* io, float* p
  * `num_shards` shards into gathered_partials[num_shards][R*num_beams][2]):
  * combines them into the rows' global lse (written to io->lse when it is not
  * NULL), scores this shard's catalog children and writes the shard's
- * canonical top-2B keys per request to shard_keys[R][2B] (zero = empty).
+ * top-2B keys per request to shard_keys[R][2B] in canonical order (key
+ * descending: score, then lower flat index parent*V+token), zero padded.
+ * The keys are the same bytes on every run and for every kernel choice.
  * io->eos_score is valid on the shard whose columns hold eos_token_id.
  * Constrained (per_beam_k == 0) steps only. */
 int32_t gr_shard_candidates(const gr_step_desc* desc, const gr_step_io* io,

@@ -171,15 +171,40 @@ def assert_close_selection(gpu: dict, ref: dict, rel_tol: float, case: Case | No
     return near_ties
 
 
-def assert_step_parity(case: Case, gpu: dict):
+# Near-ties exempted by assert_close_selection, per parity check: (label,
+# exempted, candidates compared).  conftest.py prints the totals at the end of
+# the run.
+NEAR_TIES: list = []
+
+
+def near_tie_bound(case: Case) -> int:
+    """Most boundary near-ties a seeded case may show: 1 % of its candidates,
+    at least one swapped pair per request (a last-ulp difference between the
+    float64 and the device normaliser reorders a few entries at a request's
+    boundary; a swap exempts the two entries it exchanges)."""
+    return max(2 * case.R, (case.R * 2 * case.beam_width) // 100)
+
+
+def assert_step_parity(case: Case, gpu: dict, label: str = "", max_near_ties: int | None = None):
     """Both parity levels: bit-exact given the device lse, and reference
-    arithmetic within tolerance."""
+    arithmetic within tolerance.  Returns the near-ties the reference level
+    exempted, which must stay within near_tie_bound (or max_near_ties)."""
     assert gpu["err"] == 0, f"device error word {gpu['err']:#x}"
     exact = oracle_step(case, arith="device", lse_override=gpu["lse"])
     assert_bit_exact(gpu, exact)
     ref = oracle_step(case, arith="reference")
     tol = 1e-5 if case.dtype == "f32" else 2e-3
-    return assert_close_selection(gpu, ref, rel_tol=tol, case=case)
+    ties = assert_close_selection(gpu, ref, rel_tol=tol, case=case)
+    total = int(np.sum(ref["cand_parent"] >= 0))
+    NEAR_TIES.append((label or _current_test(), ties, total))
+    bound = near_tie_bound(case) if max_near_ties is None else max_near_ties
+    assert ties <= bound, f"{ties} near-ties exempted at the boundary (bound {bound})"
+    return ties
+
+
+def _current_test() -> str:
+    import os
+    return os.environ.get("PYTEST_CURRENT_TEST", "?").split(" ")[0]
 
 
 def next_inputs(case: Case, gpu: dict, logits32_next: np.ndarray) -> Case:

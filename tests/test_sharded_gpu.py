@@ -13,6 +13,16 @@ from vllm_gr_ehaleva_b200.synthetic import initial_cum
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True, params=["auto", "ws", "stream"])
+def step_kernel(request, monkeypatch):
+    """Run every case through each step kernel choice: the automatic one (the
+    warp-specialised kernel for phase 1, the streaming kernel for phase 2),
+    the warp-specialised kernel for both phases, and the streaming kernel for
+    both."""
+    monkeypatch.setenv("GR_BEAM_KERNEL", request.param)
+    return request.param
+
+
 def sharded_gpu_step(case: Case, shards: int, device="cuda") -> dict:
     import torch
     from vllm_gr_ehaleva_b200 import sharded as SH
@@ -109,3 +119,67 @@ def test_sharded_cfg5_geometry():
         got = sharded_gpu_step(case, 8)
         assert_step_parity(case, got)
         case = next_inputs(case, got, make_logits(R, NB, V, 4.0, 60 + step, "bf16"))
+
+
+@pytest.fixture(scope="module")
+def cfg5_catalog():
+    # BASELINE cfg5's catalog: cfg2's 1M-item 3-level semantic IDs, codebook 8192, Zipf(1.1)
+    from vllm_gr_ehaleva_b200.synthetic import make_catalog
+    return make_catalog(1_000_000, 3, 8192, 152064, 1.1, seed=1)
+
+
+def _cfg5_case(cat, R=1, seed=5):
+    R, NB, B, V = R, 1024, 1024, 152064
+    return Case(logits32=make_logits(R, NB, V, 4.0, seed, "bf16"), dtype="bf16", cum=initial_cum(R, NB),
+                node=np.full((R, NB), cat.start_node, np.int32), beam_width=B, vocab_size=V, csr=cat.csr,
+                hist=np.full((R, NB, 1), cat.sid_begin, np.int32))
+
+
+@pytest.mark.slow
+def test_sharded_cfg5_true_geometry(cfg5_catalog):
+    # cfg5 as BASELINE states it, on one request: B = 1024 beams, V = 152064 in
+    # 8 shards of 19008 columns, the 1M-item catalog; root then level 1
+    case = _cfg5_case(cfg5_catalog)
+    for step in range(2):
+        got = sharded_gpu_step(case, 8)
+        assert_step_parity(case, got)
+        case = next_inputs(case, got, make_logits(case.R, case.NB, case.vocab_size, 4.0, 70 + step, "bf16"))
+
+
+def test_shard_keys_identical_across_kernels(cfg5_catalog, step_kernel):
+    # phase 2 on cfg5's catalog-heavy shards (6 and 7 hold every level-1 code):
+    # the shard's top-2B keys are the same bytes whichever step kernel scores them
+    import os
+
+    import torch
+    from vllm_gr_ehaleva_b200 import sharded as SH
+    if step_kernel != "auto":
+        pytest.skip("compares the kernels itself")
+    case = _cfg5_case(cfg5_catalog, R=1, seed=8)
+    V, S = case.vocab_size, 8
+    VL = V // S
+    full = to_device_logits(case, "cuda")
+    cum = torch.from_numpy(case.cum).cuda()
+    node = torch.from_numpy(case.node).cuda()
+    csr = tuple(torch.from_numpy(a).cuda() for a in (case.csr.row_ptr, case.csr.child_tok, case.csr.child_node))
+    kw = dict(beam_width=case.beam_width, csr=csr, vocab_size=V)
+    parts = torch.stack([SH.lse_partials(full[:, k * VL:(k + 1) * VL], cum, node, vocab_offset=k * VL, **kw)
+                         for k in range(S)])
+    keys = {}
+    for kern in ("ws", "stream"):
+        os.environ["GR_BEAM_KERNEL"] = kern
+        for k in (6, 7):
+            kk, _, _, err = SH.shard_candidates(full[:, k * VL:(k + 1) * VL], cum, node, parts, vocab_offset=k * VL,
+                                                **kw)
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0
+            keys[(kern, k)] = kk.cpu().numpy()
+    os.environ["GR_BEAM_KERNEL"] = "auto"
+    for k in (6, 7):
+        a, b = keys[("ws", k)], keys[("stream", k)]
+        assert np.array_equal(a, b), f"shard {k}: phase-2 keys differ between the kernels"
+        # canonical order: keys descending (as unsigned), zero padding last
+        u = a.view(np.uint64)
+        for r in range(u.shape[0]):
+            nz = u[r][u[r] != 0]
+            assert np.all(nz[:-1] > nz[1:]) and np.all(u[r][len(nz):] == 0)

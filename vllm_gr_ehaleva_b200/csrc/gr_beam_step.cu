@@ -115,6 +115,7 @@ struct Params {
   int tab_cap;   // penalty table entries (>= the history length)
   int win_bytes; // child window bytes (0: no constrained rows in the step)
   int partial_only;   // 1: write (max, sumexp) partials only (vocab-sharded phase 1)
+  int stall_copies;   // test hook: the producer issues no copies, so the bounded waits run out
   float2* partials;
   const float* lse_in;            // vocab-sharded phase 2: the rows' global normaliser (no streaming)
   unsigned long long* keys_out;   // merge writes the sorted top-2B keys [R][2B] (zero padded) instead
@@ -612,12 +613,16 @@ struct Step {
     static_assert(kBatch == kThreads * 8, "dense path: one 8-entry group per thread per batch");
     bool dense_done = false;
     constexpr int kG = 4;   // the one-pass dense scan covers kG * kBatch window entries
+    // an EOS child scores -inf in the pool: the value bound then takes one child more
+    const int eos_j = (P.eos >= 0) ? P.eos - c.lo_tok : -1;
+    const int ksel = P.k2 + ((eos_j >= 0 && eos_j < deg) ? 1 : 0);
     for (int attempt = 0; attempt < 2 && !dense_done && dense_window && d0 + deg <= kG * kBatch; ++attempt) {
-      if ((S.v->thr_key == 0ull || attempt == 1) && deg > P.k2) {
-        // a weak bound: tighten it with the row's own 2B-th best child value.
-        // Scores are monotone in the value, so every child scoring at least
-        // that value's score is kept, and at least 2B children do.
-        const Cut vc = cta_radix_select([this, d0](int j) { return win_value_key(d0 + j, j); }, deg, P.k2, S.sel);
+      if ((S.v->thr_key == 0ull || attempt == 1) && deg > ksel) {
+        // a weak bound: tighten it with the row's own 2B-th best child value
+        // (the (2B+1)-th when one child is EOS).  Scores are monotone in the
+        // value, so every child scoring at least that value's score is kept,
+        // and at least 2B children other than EOS do.
+        const Cut vc = cta_radix_select([this, d0](int j) { return win_value_key(d0 + j, j); }, deg, ksel, S.sel);
         if (threadIdx.x == 0) {
           const float xt = value_of_key(vc.floor_key());
           const float st = __fadd_rn(__fadd_rn(c.cum, __fsub_rn(xt, lse)), 0.0f);
@@ -633,7 +638,6 @@ struct Step {
       // dense children score as the window value (no temperature, no table):
       // the key arithmetic runs branch-free for all of them; EOS keeps a -inf
       // score and records its completion score
-      const int eos_j = (P.eos >= 0) ? P.eos - c.lo_tok : -1;
       uint32_t pm[kG];
       uint32_t cnt_t = 0;
 #pragma unroll
@@ -815,8 +819,76 @@ struct Step {
     }
   }
 
+  // The largest log-prob-domain value below y that a column of this row can
+  // hold.  A streamed row that dropped columns kept every column whose key
+  // (value, then lower flat index) beats the dropped ones, so a dropped column
+  // has the kept minimum value y_last (and a larger flat index than the kept
+  // columns of that value) or a value at most value_below(y_last).  Raw 2-byte
+  // logits step to the next lower value of their type; otherwise (f32 logits,
+  // or processed values x / T) to the next lower float32.
+  __device__ __forceinline__ float value_below(float y) const {
+    if (!(y > -kInf)) return y;                      // -inf (nothing below) or NaN
+    if constexpr (ES == 2) {
+      if (P.mode != kModeProcessed) {
+        uint32_t h;
+        if constexpr (std::is_same_v<TL, __nv_bfloat16>) h = __float_as_uint(y) >> 16;
+        else h = __half_as_ushort(__float2half_rn(y));
+        const uint32_t sign = 0x8000u;
+        h = ((h & 0x7FFFu) == 0u) ? (sign | 1u) : ((h & sign) ? h + 1u : h - 1u);
+        if constexpr (std::is_same_v<TL, __nv_bfloat16>) return __uint_as_float(h << 16);
+        else return __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
+      }
+    }
+    const uint32_t u = __float_as_uint(y);
+    if ((u & 0x7FFFFFFFu) == 0u) return -__uint_as_float(1u);   // -0 / +0 -> the smallest negative
+    return __uint_as_float((u & 0x80000000u) ? u + 1u : u - 1u);
+  }
+
+  // Exact top-k of the row's columns from global memory, keyed by score
+  // (cum + (y - lse), EOS at -inf) or, with lp_only, by log-prob (y - lse):
+  // for streamed rows whose dropped columns could tie the kept boundary after
+  // rounding.  Keys beating a running bound (the k-th key of a k-subset, a
+  // lower bound of the row's k-th) are appended in batches; the list is cut
+  // back to k whenever the next batch might not fit.
+  __device__ void rescan_row(const RowCtx& c, float lse, int k, bool lp_only) {
+    const Smem S = smem_view(P);
+    csync();
+    if (threadIdx.x == 0) {
+      S.v->cnt = 0;
+      S.v->overflow = 0;
+    }
+    csync();
+    constexpr int kMaxPer = kBatch / kThreads;
+    // columns per thread per batch: a batch must fit beside the k kept keys
+    const int per = max(1, min(kMaxPer, (kKeyCap - k) / kThreads));
+    const int nb = per * kThreads;
+    const uint32_t fb = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V) + static_cast<uint32_t>(P.voff);
+    uint64_t thr = 0ull;
+    for (int base = 0; base < P.VL; base += nb) {
+      uint64_t kv[kMaxPer];
+      uint32_t mask = 0;
+#pragma unroll
+      for (int i = 0; i < kMaxPer; ++i) {
+        kv[i] = 0ull;
+        const int tl = base + i * kThreads + static_cast<int>(threadIdx.x);
+        if (i < per && tl < P.VL) {
+          const float lp = __fsub_rn(exact_y(c, load_logit(c, tl), tl), lse);
+          float sc = lp_only ? lp : __fadd_rn(c.cum, lp);
+          if (!lp_only && P.voff + tl == P.eos) sc = -kInf;
+          kv[i] = make_key(sc, fb + static_cast<uint32_t>(tl));
+          if (kv[i] >= thr) mask |= 1u << i;
+        }
+      }
+      warp_append_n<kMaxPer>(mask, kv, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
+      csync();
+      if (base + nb < P.VL && static_cast<int>(S.v->cnt) > kKeyCap - nb) thr = shrink_to(k).floor_key();
+    }
+    if (static_cast<int>(S.v->cnt) > k) shrink_to(k);
+  }
+
   // Streamed rows: convert the kept value-keys (ord(y) | ~flat) into score keys.
-  // Returns false if the streamed boundary could hide a candidate.
+  // A row that dropped columns is read again exactly when a dropped column
+  // could score as high as the row's 2B-th candidate.
   __device__ void unconstrained_candidates(const RowCtx& c, float lse) {
     const Smem S = smem_view(P);
     // the kept set holds the row's best kk value-keys (all of them if nothing was discarded)
@@ -845,13 +917,16 @@ struct Step {
     }
     csync();
     if (n > P.k2) {
+      // the row's 2B-th key bounds the request (any 2B of its candidates do)
       const Cut cut = shrink_to(P.k2);
-      if (P.K == 0) raise_tau(c.r, cut.floor_key());   // the row's 2B-th key bounds the request
+      if (P.K == 0) raise_tau(c.r, cut.floor_key());
     }
     if (discarded && n > 0) {
-      const float s_last = __fadd_rn(c.cum, __fsub_rn(y_last, lse));
+      // a dropped column scores at most s_below; equal to the 2B-th score, it
+      // might precede it by flat index: take the row's exact top-2B instead
+      const float s_below = __fadd_rn(c.cum, __fsub_rn(value_below(y_last), lse));
       const float s_kth = key_score(min_key_of_list());
-      if (threadIdx.x == 0 && !(s_last < s_kth)) atomicOr(P.err, GR_DEVERR_TIE_BOUNDARY);
+      if (!(s_below < s_kth)) rescan_row(c, lse, P.k2, false);
     }
   }
 
@@ -908,9 +983,13 @@ struct Step {
     const int K = min(P.K, n);
     if (n > K) shrink_to(K);
     n = min(static_cast<int>(S.v->cnt), kKeyCap);
-    const uint64_t kth = (n > 0) ? min_key_of_list() : 0ull;
-    if (discarded && n > 0) {
-      if (threadIdx.x == 0 && !(__fsub_rn(y_last, lse) < key_score(kth))) atomicOr(P.err, GR_DEVERR_TIE_BOUNDARY);
+    uint64_t kth = (n > 0) ? min_key_of_list() : 0ull;
+    if (discarded && n > 0 && !(__fsub_rn(value_below(y_last), lse) < key_score(kth))) {
+      // a dropped column might tie the K-th log-prob and precede it by token:
+      // the row's exact top-K instead
+      rescan_row(c, lse, P.K, true);
+      n = min(static_cast<int>(S.v->cnt), kKeyCap);
+      kth = (n > 0) ? min_key_of_list() : 0ull;
     }
     // dedup against the sampled token (vllm_gr/logprobs.py:47-52)
     if (sampled_tl >= 0) {
@@ -1173,7 +1252,7 @@ __device__ __forceinline__ void produce(const Params& P, int my_n, unsigned char
   int stage = 0;
   uint32_t round = 0;
   long long fills = 0;
-  for (int it = 0; it < my_n; ++it) {
+  for (int it = 0; it < (P.stall_copies ? 0 : my_n); ++it) {
     const int row = row_of_iter(P, it);
     const Geom g = row_geom<ES, SB>(P, row);
     const int nch = stream_skipped(P, __ldg(P.meta + static_cast<size_t>(row) * kMetaWords + kMNode)) ? 0 : g.nchunks;
@@ -2016,12 +2095,6 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     k = min(k, static_cast<int>(M.cnt[1]));
   }
   GR_MPROF();
-  if (P.keys_out) {
-    // vocab-sharded phase 2: this shard's top-2B keys, unordered (the final
-    // merge sorts), zero padded
-    for (int i = tid; i < k2; i += kThreads) P.keys_out[static_cast<size_t>(r) * k2 + i] = (i < k) ? M.top[i] : 0ull;
-    return;
-  }
   // ---- descending order: rank sort for small k, bitonic otherwise
   if (k <= kThreads) {
     const uint64_t mine = (tid < k) ? M.top[tid] : 0ull;
@@ -2045,6 +2118,12 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
     else cta_bitonic_sort_desc(M.keys, P2);
   }
   GR_MPROF();
+  if (P.keys_out) {
+    // vocab-sharded phase 2: this shard's top-2B keys in canonical order (key
+    // descending), zero padded: the same bytes whichever step kernel ran
+    for (int i = tid; i < k2; i += kThreads) P.keys_out[static_cast<size_t>(r) * k2 + i] = (i < k) ? M.keys[i] : 0ull;
+    return;
+  }
   // ---- outputs: kO candidates per thread at a time, every load of a batch
   // issued before any of them is used
   const int B = P.B, T = P.T;
@@ -2215,6 +2294,15 @@ static int validate(const gr_step_desc* d) {
   return GR_OK;
 }
 
+// Test hook (GR_TEST_STALL_COPIES=1): the step kernels' producers issue no
+// bulk copies, so the consumers' bounded waits run out and the call reports
+// GR_DEVERR_TIMEOUT instead of its result.  Tests use it to check the
+// expiry path; nothing else sets it.
+static int stall_copies_requested() {
+  const char* e = std::getenv("GR_TEST_STALL_COPIES");
+  return (e != nullptr && e[0] == '1') ? 1 : 0;
+}
+
 static void fill_params(Params& P, const gr_step_desc* d, const gr_step_io* io) {
   P.R = d->num_requests;
   P.NB = d->num_beams;
@@ -2264,6 +2352,7 @@ static void fill_params(Params& P, const gr_step_desc* d, const gr_step_io* io) 
   P.tab_cap = P.pen ? ((d->hist_len > 0 ? d->hist_len : 1) + 31) / 32 * 32 : 0;
   P.win_bytes = (d->num_nodes > 0 && P.K == 0) ? kWinBytes : 0;
   P.partial_only = 0;
+  P.stall_copies = stall_copies_requested();
   P.partials = nullptr;
   P.lse_in = nullptr;
   P.keys_out = nullptr;

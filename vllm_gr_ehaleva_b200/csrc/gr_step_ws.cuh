@@ -186,7 +186,7 @@ __device__ void ws_produce(const Params& P) {
                           static_cast<uintptr_t>(row) * static_cast<uintptr_t>(P.row_stride) * ES;
       int wlo = 1, whi = 0;
       uint32_t wbytes = 0;
-      if (P.K == 0 && !P.partial_only && node >= 0 && c1 > c0) {
+      if (P.K == 0 && !P.partial_only && !P.stall_copies && node >= 0 && c1 > c0) {
         const int lo = max(lt - P.voff, 0), hi = min(ht - P.voff, P.VL - 1);
         if (lo <= hi) {
           const uintptr_t body0 = (a + 15) & ~uintptr_t(15);
@@ -214,7 +214,8 @@ __device__ void ws_produce(const Params& P) {
     if (lane == 0) {
       mbar_arrive(&W.recfull[slot]);   // release: the record (every lane's word) and the window bounds
       const Geom g = row_geom<ES, ws::kStage>(P, row);
-      const int nchunks = P.lse_in ? 0 : g.nchunks;   // a given normaliser needs no stream
+      // a given normaliser needs no stream (the test hook issues none either)
+      const int nchunks = (P.lse_in || P.stall_copies) ? 0 : g.nchunks;
       for (int ch = 0; ch < nchunks; ++ch) {
         if (fills >= P.stages &&
             !mbar_wait_bounded(&S.empty[stage], (round - 1u) & 1u, &S.v->abort)) {

@@ -176,10 +176,26 @@ def _prepare(logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor, *, bea
     io.eos_score, io.hist_out, io.lse, io.err = _ptr(out.eos_score), _ptr(out.hist_out), _ptr(out.lse), _ptr(out.err)
     nbytes = workspace_size(desc)
     ws = (workspace or Workspace(device)).get(nbytes)
-    s = stream if stream is not None else torch.cuda.current_stream(device)
     # the tensors the io pointers refer to stay alive with the returned tuple
     keep = (logits, cum, node, hist, row_ptr, child_tok, child_node, temps, reps, press, freqs)
+    s = _launch_stream(stream, device, keep + tuple(vars(out).values()) + (ws,))
     return desc, io, out, ws, s, keep
+
+
+def _launch_stream(stream: Optional[torch.cuda.Stream], device, tensors) -> torch.cuda.Stream:
+    """The stream the library calls run on.  The inputs, their converted
+    copies and the outputs were made on the current stream: a different
+    launch stream first waits for the current one, and every tensor the call
+    reads or writes is recorded as used on it, so that the caching allocator
+    does not hand its memory out again before the call's kernels are done."""
+    cur = torch.cuda.current_stream(device)
+    if stream is None or stream == cur:
+        return cur
+    stream.wait_stream(cur)
+    for t in tensors:
+        if isinstance(t, torch.Tensor) and t.is_cuda:
+            t.record_stream(stream)
+    return stream
 
 
 def beam_step(logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor, *, beam_width: int,

@@ -27,7 +27,7 @@ from typing import Callable, Optional
 import torch
 
 from . import _lib
-from .sample.beam_search_sampler import BeamStepOutput, Workspace, _prepare
+from .sample.beam_search_sampler import BeamStepOutput, Workspace, _launch_stream, _prepare
 
 __all__ = ["lse_partials", "shard_candidates", "merge_candidates", "sharded_beam_step", "torch_all_gather"]
 
@@ -42,6 +42,7 @@ def lse_partials(local_logits: torch.Tensor, cum: torch.Tensor, node: torch.Tens
     desc, io, out, ws, s, _keep = _prepare(local_logits, cum, node, **kw)
     R, NB = out.lse.shape
     partials = torch.empty((R * NB, 2), dtype=torch.float32, device=local_logits.device)
+    s = _launch_stream(kw.get("stream"), local_logits.device, (partials,))
     _call("gr_lse_partials", lib.gr_lse_partials, ctypes.byref(desc), ctypes.byref(io),
           ctypes.c_void_p(partials.data_ptr()), ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel()),
           ctypes.c_void_p(s.cuda_stream))
@@ -59,6 +60,7 @@ def shard_candidates(local_logits: torch.Tensor, cum: torch.Tensor, node: torch.
     S = int(gathered_partials.shape[0])
     gathered_partials = gathered_partials.to(torch.float32).contiguous()
     keys = torch.empty((R, k2), dtype=torch.int64, device=local_logits.device)
+    s = _launch_stream(kw.get("stream"), local_logits.device, (gathered_partials, keys))
     _call("gr_shard_candidates", lib.gr_shard_candidates, ctypes.byref(desc), ctypes.byref(io),
           ctypes.c_void_p(gathered_partials.data_ptr()), ctypes.c_int32(S), ctypes.c_void_p(keys.data_ptr()),
           ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel()), ctypes.c_void_p(s.cuda_stream))
@@ -72,6 +74,7 @@ def merge_candidates(local_logits: torch.Tensor, cum: torch.Tensor, node: torch.
     desc, io, out, ws, s, _keep = _prepare(local_logits, cum, node, **kw)
     S = int(gathered_keys.shape[0])
     gathered_keys = gathered_keys.to(torch.int64).contiguous()
+    s = _launch_stream(kw.get("stream"), local_logits.device, (gathered_keys,))
     _call("gr_merge_candidates", lib.gr_merge_candidates, ctypes.byref(desc), ctypes.byref(io),
           ctypes.c_void_p(gathered_keys.data_ptr()), ctypes.c_int32(S), ctypes.c_void_p(ws.data_ptr()),
           ctypes.c_size_t(ws.numel()), ctypes.c_void_p(s.cuda_stream))
