@@ -14,15 +14,20 @@ bandwidth in MEASURED_PEAKS.json.  Logits are synthetic N(0, sigma^2) from a
 seeded torch.Generator, each step's logits (>= 1.2 GB) exceed the 126 MB L2,
 so no flush is needed between iterations.
 
---gpus N (under torchrun): requests are sharded, every rank runs its own
-batch of the configured size (weak scaling, no collective on the data path);
-the time is the max over ranks of the device-timed region.
+--gpus N (under torchrun): requests are sharded, no collective on the data
+path; the time is the max over ranks of the device-timed region.  cfg1, cfg2
+and cfg4: every rank runs its own batch of the configured size (weak
+scaling).  cfg3: BASELINE's batch of 128 requests is split over the ranks
+(strong scaling, 128 / N requests per rank).
 --config cfg5 --gpus N (under torchrun): the vocabulary-sharded step instead:
-every rank holds V/N logit columns of the same requests and the ranks
-exchange per-row partials and per-request top-2B keys by NCCL all-gathers
-(strong scaling: the job is fixed, per-rank bytes shrink with N).
+every rank holds V/N logit columns of the same requests (by default the
+strided split: rank k holds tokens k, k + N, ...) and the ranks exchange
+per-row partials and per-request top-2B keys by NCCL all-gathers (strong
+scaling: the job is fixed, per-rank bytes shrink with N); the line splits the
+step's time into its phases and the two all-gathers.
 --impl reference: the CPU restatement of the reference's step (the oracle
-port) on the host cores, on a bounded sample of the same workload.
+port) on the host cores, on the same chain of levels with beams carried
+forward (all requests of cfg2; a stated sample of larger configurations).
 """
 from __future__ import annotations
 
@@ -56,6 +61,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--requests", type=int, default=None, help="override requests per GPU")
+    ap.add_argument("--split", default="strided", choices=["strided", "contiguous"],
+                    help="vocab-sharded cfg5: how the lm_head's columns are dealt to the ranks")
+    ap.add_argument("--catalog-cache", default=None,
+                    help="directory to keep built synthetic catalogs in (reused by later runs of the same call)")
     ap.add_argument("--component", default="step", choices=["step", "suffix_kv", "wire", "remux", "hook"],
                     help="suffix_kv: the suffix KV gather of the attention pass; wire: the step message (host); "
                          "remux: the worker's logprobs remux; hook: the worker-side step over cfg2 sessions")
@@ -124,16 +133,60 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ workload
-def build_workload(cfg_name: str, requests: int | None, device):
+# Configurations whose batch is split over the ranks (strong scaling); the
+# others give every rank the configured batch (weak scaling).
+STRONG = {"cfg3"}
+
+
+def requests_per_rank(cfg_name: str, requests: int | None, world: int) -> int:
+    if requests:
+        return requests
+    total = CONFIGS[cfg_name]["requests"]
+    if cfg_name in STRONG:
+        if total % world:
+            raise SystemExit(f"{total} requests do not split over {world} ranks")
+        return total // world
+    return total
+
+
+def catalog_for(cfg, cache_dir=None):
+    """The configuration's synthetic catalog (seed 1), optionally kept in
+    cache_dir between runs."""
+    if cache_dir:
+        import hashlib
+        from vllm_gr_ehaleva_b200.catalog import CSRTrie
+        from vllm_gr_ehaleva_b200.synthetic import SyntheticCatalog
+        src = open(os.path.join(ROOT, "vllm_gr_ehaleva_b200", "synthetic.py"), "rb").read()
+        key = hashlib.sha1(repr((cfg["items"], cfg["levels"], cfg["codebook"], cfg["vocab"], cfg["zipf"])).encode()
+                           + src).hexdigest()[:16]
+        path = os.path.join(cache_dir, f"catalog_{key}.npz")
+        if os.path.exists(path):
+            z = np.load(path)
+            m = [int(v) for v in z["meta"]]
+            return SyntheticCatalog(csr=CSRTrie(z["row_ptr"], z["child_tok"], z["child_node"]), vocab_size=m[0],
+                                    levels=m[1], codebook=m[2], num_items=m[3], sid_begin=m[4], sid_end=m[5],
+                                    start_node=m[6])
+    cat = make_catalog(cfg["items"], cfg["levels"], cfg["codebook"], cfg["vocab"], cfg["zipf"], seed=1)
+    if cache_dir:
+        os.makedirs(cache_dir, exist_ok=True)
+        tmp = path + f".{os.getpid()}.tmp.npz"
+        np.savez(tmp, row_ptr=cat.csr.row_ptr, child_tok=cat.csr.child_tok, child_node=cat.csr.child_node,
+                 meta=np.array([cat.vocab_size, cat.levels, cat.codebook, cat.num_items, cat.sid_begin,
+                                cat.sid_end, cat.start_node], np.int64))
+        os.replace(tmp, path)
+    return cat
+
+
+def build_workload(cfg_name: str, requests: int | None, device, world: int = 1, cache_dir=None):
     import torch
     from vllm_gr_ehaleva_b200.synthetic import logits_torch
     cfg = dict(CONFIGS[cfg_name])
-    R = requests or cfg["requests"]
+    R = requests_per_rank(cfg_name, requests, world)
     B, V = cfg["beams"], cfg["vocab"]
     dtype = {"bf16": torch.bfloat16, "f32": torch.float32}[cfg["dtype"]]
     wl = {"cfg": cfg, "R": R, "B": B, "V": V, "dtype": dtype}
     if cfg["levels"]:
-        cat = make_catalog(cfg["items"], cfg["levels"], cfg["codebook"], V, cfg["zipf"], seed=1)
+        cat = catalog_for(cfg, cache_dir)
         wl["catalog"] = cat
         wl["levels"] = cfg["levels"]
         wl["csr_dev"] = (torch.from_numpy(cat.csr.row_ptr).to(device), torch.from_numpy(cat.csr.child_tok).to(device),
@@ -143,7 +196,22 @@ def build_workload(cfg_name: str, requests: int | None, device):
         wl["levels"] = 2        # unconstrained: alternate two logits buffers
         wl["csr_dev"] = None
     nbuf = wl["levels"]
-    wl["logits"] = [logits_torch(R * B, V, cfg["sigma"], seed=100 + i, dtype=dtype, device=device) for i in range(nbuf)]
+    rows = R * B
+    if rows * V * 4 <= (4 << 30):
+        wl["logits"] = [logits_torch(rows, V, cfg["sigma"], seed=100 + i, dtype=dtype, device=device)
+                        for i in range(nbuf)]
+    else:
+        # large batches (cfg3 on few GPUs): drawn in blocks of rows so that the
+        # float32 draw never holds more than 4 GB next to the kept buffers
+        per = max(1, (4 << 30) // (V * 4))
+        wl["logits"] = []
+        for i in range(nbuf):
+            buf = torch.empty((rows, V), dtype=dtype, device=device)
+            for j, r0 in enumerate(range(0, rows, per)):
+                r1 = min(rows, r0 + per)
+                buf[r0:r1] = logits_torch(r1 - r0, V, cfg["sigma"], seed=100 + i + 1000 * j, dtype=dtype,
+                                          device=device)
+            wl["logits"].append(buf)
     return wl
 
 
@@ -219,7 +287,7 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     device = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(device)
-    wl = build_workload(args.config, args.requests, device)
+    wl = build_workload(args.config, args.requests, device, world, args.catalog_cache)
     R, B = wl["R"], wl["B"]
     kw = step_kwargs(wl)
     ws = Workspace(device)
@@ -286,7 +354,8 @@ def run_ours(args):
     per_level_ms = [round(float(np.mean(per_step_ms[i::levels])), 5) for i in range(min(levels, args.steps))]
     per_level_range = [[round(float(np.min(per_step_ms[i::levels])), 5), round(float(np.max(per_step_ms[i::levels])), 5)]
                        for i in range(min(levels, args.steps))]
-    achieved = float(np.mean([b / (ms * 1e-3) for b, ms in zip(steps_bytes, per_step_ms)])) / 1e9
+    # all bytes of the timed steps over their summed device time
+    achieved = float(np.sum(steps_bytes)) / (float(np.sum(per_step_ms)) * 1e-3) / 1e9
     peak, peak_kind = peaks()
 
     # ---- end to end through the public API with host buffers
@@ -302,9 +371,10 @@ def run_ours(args):
     res = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": round(elapsed_ms / args.steps, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if args.config in STRONG else "weak", "vs_baseline": None,
         "dtype": wl["cfg"]["dtype"], "data": "synthetic (seeded N(0, sigma^2) logits, Zipf catalog)",
-        "config": {"workload": args.config, "requests_per_gpu": R, "beam_width": B, "vocab": wl["V"],
+        "config": {"workload": args.config, "requests_per_gpu": R, "requests_total": world * R,
+                   "beam_width": B, "vocab": wl["V"],
                    "catalog_items": None if wl["catalog"] is None else wl["catalog"].num_items,
                    "levels": wl["cfg"]["levels"], "logprobs_mode": wl["cfg"]["mode"],
                    "parallelism": f"request-sharded x{world}" if world > 1 else "single GPU",
@@ -345,7 +415,10 @@ def run_e2e(args, wl, kw, ws, device, world):
     import torch
     from vllm_gr_ehaleva_b200.sample import beam_step
     R, B = wl["R"], wl["B"]
-    host_logits = [x.cpu().pin_memory() for x in wl["logits"]]
+    # one pinned host copy of a step's logits, sent again every step (the
+    # inputs' values do not change the work; one buffer keeps large batches
+    # within host memory)
+    host_logits = wl["logits"][0].cpu().pin_memory()
     dev_buf = torch.empty_like(wl["logits"][0])
     cum0, node0, hist0 = initial_state(wl, device)
     levels = wl["levels"]
@@ -355,8 +428,7 @@ def run_e2e(args, wl, kw, ws, device, world):
     steps = max(3, min(args.steps, 10))
 
     def one(i, cum, node, hist):
-        lvl = i % levels
-        dev_buf.copy_(host_logits[lvl], non_blocking=True)
+        dev_buf.copy_(host_logits, non_blocking=True)
         out = beam_step(dev_buf, cum, node, hist=hist, workspace=ws, **kw)
         for k in host_out:
             host_out[k].copy_(getattr(out, k), non_blocking=True)
@@ -461,39 +533,109 @@ def cpu_model():
     return "unknown"
 
 
+def cpu_chain_logits(cfg, n_req: int, threads: int, seed: int = 0):
+    """Host logits of n_req requests in the storage dtype (bf16 as its bit
+    patterns), drawn one request per task outside any timing."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle.restated import f32_to_bf16_bits
+    B, V = cfg["beams"], cfg["vocab"]
+
+    def draw(r):
+        rng = np.random.default_rng(seed * 100003 + r)
+        x = (rng.standard_normal((B, V), dtype=np.float32) * np.float32(cfg["sigma"]))
+        return f32_to_bf16_bits(x) if cfg["dtype"] == "bf16" else x.astype(np.float32)
+
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        return list(ex.map(draw, range(n_req)))
+
+
 def run_reference(args):
-    """Reference arm: the oracle port of the reference's CPU step, all host threads."""
+    """Reference arm: the oracle port of the reference's CPU step (reference
+    arithmetic: float64 normaliser and score sums, as the reference's Python
+    loops) on all host threads, one request per task.  A step is one beam step
+    of the sampled requests at the next catalog level, the beams carried
+    forward from the previous step as in the GPU arm (root, level 1, ...,
+    then the root again); the bf16 -> float32 conversion of the logits is
+    inside the timed step (vLLM's logits.float()), their generation is not."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import restated as O
     cfg = dict(CONFIGS[args.config])
-    cat = None
-    if cfg["levels"]:
-        cat = make_catalog(cfg["items"], cfg["levels"], cfg["codebook"], cfg["vocab"], cfg["zipf"], seed=1)
+    R = cfg["requests"]
+    B, V = cfg["beams"], cfg["vocab"]
     threads = len(os.sched_getaffinity(0))
-    n_req = max(1, threads)
-    for _ in range(max(args.warmup, 0) and 1):
-        cpu_step_time(cfg, cat, 1, 1, 5.0)
-    tot_s, tot_r = 0.0, 0
-    steps = max(1, min(args.steps, 3))
-    for _ in range(steps):
-        s, d = cpu_step_time(cfg, cat, n_req, threads, 30.0)
-        tot_s += s
-        tot_r += d
-    value = tot_r / tot_s
+    # every request of cfg2 / cfg1 / cfg5; a sample of at least 32 requests (one per task) for the larger batches
+    n_req = min(R, max(32, threads))
+    cat = catalog_for(cfg, args.catalog_cache) if cfg["levels"] else None
+    levels = cfg["levels"] if cat is not None else 2
+    xs = cpu_chain_logits(cfg, n_req, threads)
+    csr = O.CSR(cat.csr.row_ptr, cat.csr.child_tok, cat.csr.child_node) if cat is not None else None
+    kw = {}
+    if cfg["mode"] == "processed":
+        kw = dict(logprobs_mode=O.PROCESSED, temperature=[cfg["temperature"]], rep_penalty=[cfg["rep"]],
+                  pres_penalty=[cfg["pres"]], freq_penalty=[cfg["freq"]])
+
+    def initial():
+        cum = initial_cum(n_req, B)
+        if cat is not None:
+            return ([cum[r:r + 1] for r in range(n_req)], [np.full((1, B), cat.start_node, np.int32)] * n_req,
+                    [np.full((1, B, 1), cat.sid_begin, np.int32)] * n_req)
+        hist = histories(n_req, B, cfg["hist"], V, seed=3)
+        return ([cum[r:r + 1] for r in range(n_req)], [np.full((1, B), -1, np.int32)] * n_req,
+                [hist[r:r + 1] for r in range(n_req)])
+
+    state = initial()
+
+    def one(r):
+        x = O.bf16_bits_to_f32(xs[r]) if cfg["dtype"] == "bf16" else xs[r]
+        return O.beam_step(x[None], state[0][r], state[1][r], csr, beam_width=B, vocab_size=V,
+                           hist_in=state[2][r], **kw)
+
+    def step(i, ex):
+        nonlocal state
+        outs = list(ex.map(one, range(n_req)))
+        if (i + 1) % levels == 0:
+            state = initial()
+        else:
+            keep_hist = cat is None      # unconstrained: the fixed-length penalty history
+            state = ([o["sel_score"] for o in outs], [o["sel_node"] for o in outs],
+                     state[2] if keep_hist else [o["hist_out"] for o in outs])
+
+    warm = max(args.warmup, 3)
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        for i in range(warm):                  # untimed steps warm the pool and the caches
+            step(i, ex)
+        state = initial()
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            step(i, ex)
+        secs = time.perf_counter() - t0
+    value = n_req * args.steps / secs
+    sample = (f"{n_req} of {R} requests" if n_req < R else f"all {R} requests") + \
+             f" x {args.steps} steps, levels cycling over {levels} (oracle/restated.py, one request per task)"
+    cfg_line = {"workload": args.config, "requests_per_gpu": R, "requests_total": R, "beam_width": B, "vocab": V,
+                "catalog_items": None if cat is None else cat.num_items, "levels": cfg["levels"],
+                "logprobs_mode": cfg["mode"], "parallelism": "single GPU",
+                "l2": "inputs larger than L2 (>= 1.2 GB logits per step), no flush"}
     res = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": 0,
-           "steps": steps, "warmup": 1, "ms_per_step": round(1e3 * tot_s / steps, 3), "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
-           "config": {"workload": args.config, "beam_width": cfg["beams"], "vocab": cfg["vocab"]},
+           "steps": args.steps, "warmup": warm, "ms_per_step": round(1e3 * secs / args.steps, 3),
+           "higher_is_better": True, "scaling": "strong" if args.config in STRONG else "weak", "vs_baseline": None,
+           "dtype": cfg["dtype"], "data": "synthetic (seeded N(0, sigma^2) logits, Zipf catalog)",
+           "config": cfg_line,
            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
-                            "sample": f"{n_req} requests x 1 root-level step per timed step",
-                            "cpu_model": cpu_model()},
+                            "sample": sample, "cpu_model": cpu_model()},
            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(res), flush=True)
 
 
 def run_sharded(args):
-    """Vocabulary-sharded step (cfg5) on N GPUs: each rank V/N columns, NCCL all-gathers."""
+    """Vocabulary-sharded step (cfg5) on N GPUs: each rank V/N columns, NCCL all-gathers.
+    With the strided split (default) rank k holds the columns of tokens k, k + N,
+    k + 2N, ... (the lm_head's rows dealt round robin once), so every rank gets
+    about 1/N of each trie node's children; --split contiguous gives rank k the
+    slice [k V/N, (k + 1) V/N)."""
     import datetime
 
     import torch
@@ -512,7 +654,9 @@ def run_sharded(args):
     if V % world:
         raise SystemExit(f"vocab {V} does not split over {world} ranks")
     VL = V // world
-    cat = make_catalog(cfg["items"], cfg["levels"], cfg["codebook"], V, cfg["zipf"], seed=1)
+    strided = args.split == "strided"
+    voff, vstride = (rank, world) if strided else (rank * VL, 1)
+    cat = catalog_for(cfg, args.catalog_cache)
     csr = tuple(torch.from_numpy(a).to(device) for a in (cat.csr.row_ptr, cat.csr.child_tok, cat.csr.child_node))
     levels = cfg["levels"]
     logits = [logits_torch(R * B, VL, cfg["sigma"], seed=1000 + 17 * lvl + rank, dtype=torch.bfloat16, device=device)
@@ -523,13 +667,15 @@ def run_sharded(args):
     stream = torch.cuda.current_stream(device)
     # one persistent stepper per fork-table length (the table grows by one token per level)
     steppers = [ShardedStepper(num_requests=R, num_beams=B, beam_width=B, vocab_size=V, vocab_local=VL,
-                               vocab_offset=rank * VL, num_shards=world, csr=csr, hist_len=1 + lvl, device=device)
+                               vocab_offset=voff, vocab_stride=vstride, num_shards=world, csr=csr,
+                               hist_len=1 + lvl, device=device)
                 for lvl in range(levels)]
 
-    def chain(n):
+    def chain(n, marks=None):
         cum, node, hist = cum0, node0, hist0
         for i in range(n):
-            out = steppers[i % levels].step(logits[i % levels], cum, node, hist)
+            out = steppers[i % levels].step(logits[i % levels], cum, node, hist,
+                                            marks=None if marks is None else marks[i])
             if (i + 1) % levels == 0:
                 cum, node, hist = cum0, node0, hist0
             else:
@@ -556,20 +702,34 @@ def run_sharded(args):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     step_ms = ms / args.steps
+    # phases timed apart in a second pass of the same steps (events between the
+    # phases, max over ranks of each phase's mean)
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(args.steps)]
+    dist.barrier()
+    chain(args.steps, marks)
+    torch.cuda.synchronize()
+    names = ["lse_partials", "allgather_partials", "shard_candidates", "allgather_keys", "merge"]
+    phase = torch.tensor([float(np.mean([m[i].elapsed_time(m[i + 1]) for m in marks])) for i in range(5)],
+                         device=device)
+    dist.all_reduce(phase, op=dist.ReduceOp.MAX)
+    phases_ms = {n: round(float(v), 5) for n, v in zip(names, phase.tolist())}
     local_bytes = R * B * VL * 2          # this rank's logits, read once per step
     peak, peak_kind = peaks()
-    achieved = local_bytes / (step_ms * 1e-3) / 1e9
+    # the HBM-bound phase is the lse-partials stream: its bytes over its own time
+    achieved = local_bytes / (phases_ms["lse_partials"] * 1e-3) / 1e9
     res = {
         "metric": METRIC, "value": round(R * args.steps / (ms * 1e-3), 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(step_ms, 5),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0, sigma^2) logits, Zipf catalog)",
         "config": {"workload": args.config, "requests": R, "beam_width": B, "vocab": V, "vocab_per_rank": VL,
-                   "parallelism": f"vocab-sharded x{world} (NCCL all-gathers)",
+                   "split": args.split,
+                   "parallelism": f"vocab-sharded x{world} (NCCL all-gathers, {args.split} columns)",
                    "l2": "per-rank logits larger than L2, no flush"},
+        "phases_ms": phases_ms,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
-                     "kernel": "whole sharded step per rank (3 phases + 2 all-gathers)",
+                     "kernel": "lse-partials stream of this rank's columns (phase 1)",
                      "algorithmic_bytes_per_launch": local_bytes},
         "gpu_launches": 8 * args.steps,
         "clocks": clk, "device_errors": err,

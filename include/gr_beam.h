@@ -52,7 +52,7 @@
 extern "C" {
 #endif
 
-#define GR_ABI_VERSION 1
+#define GR_ABI_VERSION 2
 
 typedef enum gr_status {
   GR_OK = 0,
@@ -111,6 +111,11 @@ typedef struct gr_step_desc {
                              in processed mode, the penalty history)          */
   int32_t num_nodes;      /* N: CSR trie nodes (0 if no catalog)              */
   int64_t num_edges;      /* E: CSR trie edges                                */
+  int32_t vocab_stride;   /* local column j holds token vocab_offset +
+                             j * vocab_stride (0 or 1: a contiguous slice;
+                             S with vocab_offset = k: shard k of a strided
+                             split over S ranks, tokens k, k + S, ...)      */
+  int32_t reserved;       /* 0                                                */
 } gr_step_desc;
 
 typedef struct gr_step_io {
@@ -176,16 +181,25 @@ int32_t gr_beam_step(const gr_step_desc* desc, const gr_step_io* io,
  *   - All calls share the one array: calls that may run at the same time on
  *     the GPU (different streams, different host threads) race on it and must
  *     be serialised by the caller.
+ *   - The address is kept for the life of the process: the library must not
+ *     be used across a reset of the device (cudaDeviceReset) that would move
+ *     or free the array.
  * No counterpart in the reference (an addition of this library). */
 int32_t gr_beam_step_noalloc(const gr_step_desc* desc, const gr_step_io* io, void* stream);
 
 /* ---- vocab-sharded lm_head (logit columns split over ranks) --------------
  *
- * With the lm_head split by vocabulary columns, shard k holds columns
- * [vocab_offset, vocab_offset + vocab_local) of every row (vLLM would
- * all-gather the full logits first: vllm logits_processor.py:75-86).  A step
- * becomes three calls with two all-gathers between them, all on the caller's
- * stream; every call takes the gr_beam_step workspace (same size).
+ * With the lm_head split by vocabulary columns, shard k holds the columns of
+ * tokens vocab_offset + j * vocab_stride, j < vocab_local, of every row (vLLM
+ * would all-gather the full logits first: vllm logits_processor.py:75-86):
+ * a contiguous slice (vocab_stride 1) or, with the lm_head's weight rows
+ * dealt round robin once at load time, a strided split (vocab_offset = k,
+ * vocab_stride = number of shards).  The strided split gives every shard
+ * about 1/S of each trie node's children, which sit in one contiguous token
+ * range (semantic-ID codebooks at the vocabulary's tail), so the candidate
+ * work is balanced.  A step becomes three calls with two all-gathers between
+ * them, all on the caller's stream; every call takes the gr_beam_step
+ * workspace (same size).
  *
  * Phase 1 (every shard): per-row partial (max, sum exp(y - max)) over the
  * local columns, y the log-prob domain value (processed mode: penalties and
@@ -292,7 +306,9 @@ typedef struct gr_suffix_req {
  * a beam) to totals[6].  Follows beam_attn.py:255-292 (a long uncached prefix
  * first goes through standard attention) and 319-413 (beam 0's share, then
  * `steps` per beam until the query budget runs out).  GR_ERR_BAD_DESC when a
- * request's cache_len exceeds its prefix_len after that split. */
+ * request's cache_len exceeds its prefix_len after that split, or when a
+ * record's field (uncached tokens, query tokens, beams, the running beam
+ * count) would not fit in 32 bits. */
 int32_t gr_suffix_records(int32_t num_reqs, const int64_t* q_starts, const uint8_t* mega,
                           const int32_t* prefix_len, const int32_t* cache_len, const int32_t* beam_width,
                           const int32_t* steps, int32_t block_size, gr_suffix_req* recs, int64_t* totals);

@@ -28,7 +28,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), f"{n} declared in gr_beam.h but not exported"
     assert set(_lib.EXPORTED_SYMBOLS) == set(names)
-    assert lib.gr_abi_version() == 1
+    assert lib.gr_abi_version() == 2
     assert lib.gr_status_string(-6) == b"GR_ERR_UNSUPPORTED"
 
 
@@ -38,9 +38,9 @@ def test_struct_layout_matches_header():
 #include <stddef.h>
 #include "gr_beam.h"
 int main(void) {
-  printf("%zu %zu %zu %zu %zu %zu\n", sizeof(gr_step_desc), sizeof(gr_step_io),
+  printf("%zu %zu %zu %zu %zu %zu %zu\n", sizeof(gr_step_desc), sizeof(gr_step_io),
          offsetof(gr_step_desc, row_stride), offsetof(gr_step_desc, num_edges),
-         offsetof(gr_step_io, cand_score), offsetof(gr_step_io, err));
+         offsetof(gr_step_desc, vocab_stride), offsetof(gr_step_io, cand_score), offsetof(gr_step_io, err));
   return 0;
 }
 '''
@@ -51,7 +51,8 @@ int main(void) {
         subprocess.run(["gcc", "-I", os.path.dirname(HEADER), c, "-o", exe], check=True)
         got = list(map(int, subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()))
     want = [ctypes.sizeof(_lib.StepDesc), ctypes.sizeof(_lib.StepIO), _lib.StepDesc.row_stride.offset,
-            _lib.StepDesc.num_edges.offset, _lib.StepIO.cand_score.offset, _lib.StepIO.err.offset]
+            _lib.StepDesc.num_edges.offset, _lib.StepDesc.vocab_stride.offset, _lib.StepIO.cand_score.offset,
+            _lib.StepIO.err.offset]
     assert got == want
 
 
@@ -67,6 +68,9 @@ def _desc(**kw):
     (dict(VL=1001), -2), (dict(voff=10), -2), (dict(row_stride=999), -2),
     (dict(dtype=7), -3), (dict(mode=3), -3),
     (dict(K=2000), -2), (dict(eos=1000), -2),
+    (dict(VL=100, voff=3, VS=10), 0),             # strided shard: tokens 3, 13, ..., 993
+    (dict(VL=101, voff=3, VS=10), -2),            # its last token 1003 is outside the vocabulary
+    (dict(VS=-1), -2),
     (dict(B=3000), -6),                           # 2B beyond the shared-memory key list
     (dict(NB=100000, V=100000, VL=100000, row_stride=100000), -6),   # flat index beyond 32 bits
 ])
@@ -168,4 +172,4 @@ int main(void) {
                         "-o", exe], check=True)
         r = subprocess.run([exe], capture_output=True, text=True)
     assert r.returncode == 0, r.stdout + r.stderr
-    assert r.stdout.split() == ["0", "-2", "GR_ERR_BAD_DESC", "1"]
+    assert r.stdout.split() == ["0", "-2", "GR_ERR_BAD_DESC", "2"]

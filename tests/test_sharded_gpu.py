@@ -23,14 +23,22 @@ def step_kernel(request, monkeypatch):
     return request.param
 
 
-def sharded_gpu_step(case: Case, shards: int, device="cuda") -> dict:
+def sharded_gpu_step(case: Case, shards: int, device="cuda", split: str = "contiguous") -> dict:
+    """The three phases over `shards` column shards of the case's logits:
+    contiguous slices (shard k: tokens k*V/S ..) or the strided split (shard k:
+    tokens k, k + S, k + 2S, ..., as after dealing the lm_head rows round robin)."""
     import torch
     from vllm_gr_ehaleva_b200 import sharded as SH
     R, NB, V = case.R, case.NB, case.vocab_size
     assert V % shards == 0
     VL = V // shards
     full = to_device_logits(case, device)                      # [R*NB, V]
-    local = [full[:, k * VL:(k + 1) * VL] for k in range(shards)]
+    if split == "strided":
+        local = [full[:, k::shards].contiguous() for k in range(shards)]
+        offs, vs = [k for k in range(shards)], shards
+    else:
+        local = [full[:, k * VL:(k + 1) * VL] for k in range(shards)]
+        offs, vs = [k * VL for k in range(shards)], 1
     cum = torch.from_numpy(case.cum).to(device)
     node = torch.from_numpy(case.node).to(device)
     csr = None
@@ -38,12 +46,13 @@ def sharded_gpu_step(case: Case, shards: int, device="cuda") -> dict:
         csr = tuple(torch.from_numpy(a).to(device) for a in (case.csr.row_ptr, case.csr.child_tok, case.csr.child_node))
     hist = None if case.hist is None else torch.from_numpy(case.hist).to(device)
     kw = dict(beam_width=case.beam_width, csr=csr, vocab_size=V, logprobs_mode=case.mode,
-              eos_token_id=None if case.eos < 0 else case.eos, hist=hist, temperature=case.temperature)
-    parts = [SH.lse_partials(local[k], cum, node, vocab_offset=k * VL, **kw) for k in range(shards)]
+              eos_token_id=None if case.eos < 0 else case.eos, hist=hist, temperature=case.temperature,
+              vocab_stride=vs)
+    parts = [SH.lse_partials(local[k], cum, node, vocab_offset=offs[k], **kw) for k in range(shards)]
     gathered_p = torch.stack(parts)
-    res = [SH.shard_candidates(local[k], cum, node, gathered_p, vocab_offset=k * VL, **kw) for k in range(shards)]
+    res = [SH.shard_candidates(local[k], cum, node, gathered_p, vocab_offset=offs[k], **kw) for k in range(shards)]
     gathered_k = torch.stack([r[0] for r in res])
-    outs = [SH.merge_candidates(local[k], cum, node, gathered_k, vocab_offset=k * VL, **kw) for k in range(shards)]
+    outs = [SH.merge_candidates(local[k], cum, node, gathered_k, vocab_offset=offs[k], **kw) for k in range(shards)]
     torch.cuda.synchronize()
     eos = res[0][2]
     for k in range(1, shards):
@@ -67,8 +76,9 @@ def sharded_gpu_step(case: Case, shards: int, device="cuda") -> dict:
     return got
 
 
+@pytest.mark.parametrize("split", ["contiguous", "strided"])
 @pytest.mark.parametrize("shards", [2, 4])
-def test_sharded_constrained_three_steps(shards):
+def test_sharded_constrained_three_steps(shards, split):
     cat = small_catalog()
     R, NB, B, V = 3, 16, 16, 8192
     node = np.full((R, NB), cat.start_node, np.int32)
@@ -77,12 +87,13 @@ def test_sharded_constrained_three_steps(shards):
     case = Case(logits32=make_logits(R, NB, V, 4.0, 3, "bf16"), dtype="bf16", cum=initial_cum(R, NB), node=node,
                 beam_width=B, vocab_size=V, csr=cat.csr, hist=np.full((R, NB, 1), cat.sid_begin, np.int32))
     for step in range(3):
-        got = sharded_gpu_step(case, shards)
+        got = sharded_gpu_step(case, shards, split=split)
         assert_step_parity(case, got)
         case = next_inputs(case, got, make_logits(R, NB, V, 4.0, 30 + step, "bf16"))
 
 
-def test_sharded_eos_child():
+@pytest.mark.parametrize("split", ["contiguous", "strided"])
+def test_sharded_eos_child(split):
     V, eos = 64, 5
     csr = tiny_catalog_csr([[1, 2, 3], [1, 2, 40], [1, eos], [7, 8], [1, 33]])
     start = csr.walk([1])
@@ -92,18 +103,19 @@ def test_sharded_eos_child():
     case = Case(logits32=x, dtype="f32", cum=np.array([[-1, -2, -3], [-0.5, -0.7, -4]], np.float32),
                 node=node, beam_width=B, vocab_size=V, csr=csr, eos=eos,
                 hist=np.arange(R * NB * 2, dtype=np.int32).reshape(R, NB, 2))
-    got = sharded_gpu_step(case, 2)
+    got = sharded_gpu_step(case, 2, split=split)
     assert_step_parity(case, got)
     assert np.isfinite(got["eos_score"][0, 0])
 
 
-def test_sharded_processed_temperature():
+@pytest.mark.parametrize("split", ["contiguous", "strided"])
+def test_sharded_processed_temperature(split):
     cat = small_catalog()
     R, NB, B, V = 2, 8, 8, 8192
     case = Case(logits32=make_logits(R, NB, V, 4.0, 9, "f32"), dtype="f32", cum=initial_cum(R, NB),
                 node=np.full((R, NB), cat.start_node, np.int32), beam_width=B, vocab_size=V, csr=cat.csr,
                 mode="processed_logprobs", temperature=[0.7, 1.3])
-    assert_step_parity(case, sharded_gpu_step(case, 2))
+    assert_step_parity(case, sharded_gpu_step(case, 2, split=split))
 
 
 @pytest.mark.slow
@@ -136,12 +148,15 @@ def _cfg5_case(cat, R=1, seed=5):
 
 
 @pytest.mark.slow
-def test_sharded_cfg5_true_geometry(cfg5_catalog):
+@pytest.mark.parametrize("split", ["contiguous", "strided"])
+def test_sharded_cfg5_true_geometry(cfg5_catalog, split, step_kernel):
     # cfg5 as BASELINE states it, on one request: B = 1024 beams, V = 152064 in
     # 8 shards of 19008 columns, the 1M-item catalog; root then level 1
+    if split == "contiguous" and step_kernel != "auto":
+        pytest.skip("the contiguous split runs with the automatic kernel choice only")
     case = _cfg5_case(cfg5_catalog)
     for step in range(2):
-        got = sharded_gpu_step(case, 8)
+        got = sharded_gpu_step(case, 8, split=split)
         assert_step_parity(case, got)
         case = next_inputs(case, got, make_logits(case.R, case.NB, case.vocab_size, 4.0, 70 + step, "bf16"))
 

@@ -1,7 +1,8 @@
 """Vocab-sharded step across real GPUs: one process per GPU, NCCL all-gathers
-(torch_all_gather), each rank holding a column slice of the logits.  Every
-rank's outputs must equal the oracle's full-vocabulary step (bit-exact given
-the combined lse).  Needs two GPUs; skipped otherwise."""
+(torch_all_gather), each rank holding a contiguous column slice of the logits,
+then the strided split (rank k: tokens k, k + 2, ...).  Every rank's outputs
+must equal the oracle's full-vocabulary step (bit-exact given the combined
+lse).  Needs two GPUs; skipped otherwise."""
 import os
 import socket
 
@@ -37,25 +38,32 @@ def _worker(rank, world, port, q):
                     hist=np.full((R, NB, 1), cat.sid_begin, np.int32))
         dev = torch.device("cuda", rank)
         VL = V // world
-        local = to_device_logits(case, dev)[:, rank * VL:(rank + 1) * VL]
+        full = to_device_logits(case, dev)
         csr = tuple(torch.from_numpy(a).to(dev) for a in (cat.csr.row_ptr, cat.csr.child_tok, cat.csr.child_node))
-        out = sharded_beam_step(local, torch.from_numpy(case.cum).to(dev), torch.from_numpy(case.node).to(dev),
-                                all_gather=torch_all_gather(), beam_width=B, vocab_size=V, vocab_offset=rank * VL,
-                                csr=csr, hist=torch.from_numpy(case.hist).to(dev))
-        torch.cuda.synchronize()
-        res = {k: getattr(out, k).cpu().numpy() for k in OUT_KEYS}
-        res["err"] = int(out.err.item())
-        # the persistent stepper gives the same step
         from vllm_gr_ehaleva_b200.sharded import ShardedStepper
-        stepper = ShardedStepper(num_requests=R, num_beams=NB, beam_width=B, vocab_size=V, vocab_local=VL,
-                                 vocab_offset=rank * VL, num_shards=world, csr=csr, hist_len=1,
-                                 row_stride=local.stride(0), device=dev)
-        out2 = stepper.step(local, torch.from_numpy(case.cum).to(dev), torch.from_numpy(case.node).to(dev),
-                            torch.from_numpy(case.hist).to(dev))
-        torch.cuda.synchronize()
-        res["stepper_same"] = all(np.array_equal(getattr(out2, k).cpu().numpy(), res[k])
-                                  for k in ("cand_score", "cand_token", "cand_parent", "sel_node", "hist_out"))
-        q.put((rank, res))
+        results = {}
+        for split in ("contiguous", "strided"):
+            if split == "strided":
+                local, voff, vs = full[:, rank::world].contiguous(), rank, world
+            else:
+                local, voff, vs = full[:, rank * VL:(rank + 1) * VL], rank * VL, 1
+            out = sharded_beam_step(local, torch.from_numpy(case.cum).to(dev), torch.from_numpy(case.node).to(dev),
+                                    all_gather=torch_all_gather(), beam_width=B, vocab_size=V, vocab_offset=voff,
+                                    vocab_stride=vs, csr=csr, hist=torch.from_numpy(case.hist).to(dev))
+            torch.cuda.synchronize()
+            res = {k: getattr(out, k).cpu().numpy() for k in OUT_KEYS}
+            res["err"] = int(out.err.item())
+            # the persistent stepper gives the same step
+            stepper = ShardedStepper(num_requests=R, num_beams=NB, beam_width=B, vocab_size=V, vocab_local=VL,
+                                     vocab_offset=voff, vocab_stride=vs, num_shards=world, csr=csr, hist_len=1,
+                                     row_stride=local.stride(0), device=dev)
+            out2 = stepper.step(local, torch.from_numpy(case.cum).to(dev), torch.from_numpy(case.node).to(dev),
+                                torch.from_numpy(case.hist).to(dev))
+            torch.cuda.synchronize()
+            res["stepper_same"] = all(np.array_equal(getattr(out2, k).cpu().numpy(), res[k])
+                                      for k in ("cand_score", "cand_token", "cand_parent", "sel_node", "hist_out"))
+            results[split] = res
+        q.put((rank, results))
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:
@@ -85,7 +93,10 @@ def test_sharded_step_two_gpus_nccl():
                 hist=np.full((R, NB, 1), cat.sid_begin, np.int32))
     for r in range(2):
         assert "error" not in results[r], results[r]
-        assert results[r].pop("stepper_same")
-        assert_step_parity(case, results[r])
-    for k in ("cand_token", "cand_parent", "sel_node", "hist_out"):
-        assert np.array_equal(results[0][k], results[1][k]), k
+    for split in ("contiguous", "strided"):
+        for r in range(2):
+            res = results[r][split]
+            assert res.pop("stepper_same"), split
+            assert_step_parity(case, res, label=f"nccl {split} rank {r}")
+        for k in ("cand_token", "cand_parent", "sel_node", "hist_out"):
+            assert np.array_equal(results[0][split][k], results[1][split][k]), (split, k)

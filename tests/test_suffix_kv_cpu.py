@@ -183,3 +183,20 @@ def test_c_records_equal_python_records():
         mega = [dict(prefix_len=c["prefix_len"], cache_len=0, beam_width=c["beam_width"],
                      steps=c["suffix_kv_len"])] * c["batch_size"]
         assert _c_records(mega, _q_starts(c), c["block_size"]) == suffix_records(mega, _q_starts(c), c["block_size"])
+
+
+def test_c_records_refuse_fields_beyond_32_bits():
+    # a request whose query tokens (and beams) do not fit the record's 32-bit
+    # fields is refused, not wrapped: 2^32 query tokens, 2^31 - 1 beams of one step
+    import ctypes
+    from vllm_gr_ehaleva_b200 import _lib
+    lib = _lib.load()
+    q_starts = np.array([0, 2**32], np.int64)
+    flags = np.array([1], np.uint8)
+    plen, clen = np.array([10], np.int32), np.array([0], np.int32)
+    w, st = np.array([2**31 - 1], np.int32), np.array([1], np.int32)
+    recs = (_lib.SuffixReq * 1)()
+    totals = np.zeros(6, np.int64)
+    rc = lib.gr_suffix_records(1, q_starts.ctypes.data, flags.ctypes.data, plen.ctypes.data, clen.ctypes.data,
+                               w.ctypes.data, st.ctypes.data, 16, ctypes.addressof(recs), totals.ctypes.data)
+    assert rc == -2, _lib.STATUS_NAMES.get(rc, rc)     # GR_ERR_BAD_DESC

@@ -49,6 +49,8 @@ class StepDesc(ctypes.Structure):
         ("hist_len", ctypes.c_int32),
         ("num_nodes", ctypes.c_int32),
         ("num_edges", ctypes.c_int64),
+        ("vocab_stride", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 

@@ -72,6 +72,7 @@ __device__ unsigned long long g_phase[1024][kProfSlots];
 struct Params {
   // descriptor
   int R, NB, B, V, VL, voff;
+  int vstride;   // local column j holds token voff + j * vstride
   long long row_stride;
   int mode, K, eos, T, N;
   // inputs
@@ -126,6 +127,28 @@ struct Params {
   long long slot_sr, slot_sb;
   int slot_cap;
 };
+
+// Vocabulary of the local columns: column j holds token voff + j * vstride
+// (vstride 1: a contiguous slice; vstride = shards: a strided split).
+// Local column of token t, or -1 when this shard does not hold it.
+__device__ __forceinline__ int col_of(const Params& P, int t) {
+  const int d = t - P.voff;
+  if (d < 0) return -1;
+  if (P.vstride == 1) return d < P.VL ? d : -1;
+  const int j = d / P.vstride;
+  return (j * P.vstride == d && j < P.VL) ? j : -1;
+}
+__device__ __forceinline__ int tok_of(const Params& P, int j) { return P.voff + j * P.vstride; }
+// The first local column whose token is >= t, and the last one whose token is
+// <= t (-1 when there is none).
+__device__ __forceinline__ int col_ceil(const Params& P, int t) {
+  const int d = t - P.voff;
+  return (d <= 0) ? 0 : (d + P.vstride - 1) / P.vstride;
+}
+__device__ __forceinline__ int col_floor(const Params& P, int t) {
+  const int d = t - P.voff;
+  return (d < 0) ? -1 : d / P.vstride;
+}
 
 // Shared-memory layout (dynamic shared memory).  Every piece but the ring sits
 // at a compile-time offset, so accesses need no pointer arithmetic at run time;
@@ -439,7 +462,7 @@ struct Step {
       for (int i = 0; i < N; ++i) any |= valid && !((fl >> i) & 1u) && (y[i] >= thr_e);
       if (__any_sync(0xFFFFFFFFu, any)) {
         const uint32_t fbase = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V) +
-                               static_cast<uint32_t>(P.voff + tb);
+                               static_cast<uint32_t>(tok_of(P, tb));
         uint64_t kv[N];
         uint32_t mask = 0;
 #pragma unroll
@@ -447,7 +470,7 @@ struct Step {
           kv[i] = 0;
           if (valid && !((fl >> i) & 1u) && (y[i] >= thr_e)) {
             const float ye = (P.mode == kModeProcessed && c.teff != 1.0f) ? __fdiv_rn(x[i], c.teff) : x[i];
-            kv[i] = make_key(ye, fbase + i);
+            kv[i] = make_key(ye, fbase + static_cast<uint32_t>(i * P.vstride));
             if (kv[i] >= thr_key) mask |= 1u << i;
           }
         }
@@ -589,7 +612,7 @@ struct Step {
   // token and the child node at c0 + j without a search.
   __device__ __forceinline__ uint64_t child_key(const RowCtx& c, int tok, int j, float x, float lse,
                                                 uint32_t fb) const {
-    const float y = exact_y(c, x, tok - P.voff);
+    const float y = exact_y(c, x, col_of(P, tok));
     float sc = __fadd_rn(c.cum, __fsub_rn(y, lse));
     if (tok == P.eos) {
       if (P.eos_score) P.eos_score[c.row] = sc;
@@ -607,22 +630,33 @@ struct Step {
     // first; only the (rare) passers build keys and take part in the append.
     // An exact float test is enough: key >= thr implies score >= score(thr).
     const bool processed_div = (P.mode == kModeProcessed) && (c.excl || c.teff != 1.0f);
-    const int first = c.lo_tok - P.voff;
-    const bool dense_window = c.dense && !processed_div && first >= c.wlo && first + deg - 1 <= c.whi;
-    const int d0 = first - c.wlo;               // window index of the first child
+    // A dense node's children are the tokens lo_tok .. lo_tok + deg - 1; this
+    // shard holds those in local columns first_l .. last_l.  Window entry w is
+    // local column wlo + w, the child of index jb + w * vs (outside [0, deg):
+    // not a child).
+    const int vs = P.vstride;
+    const int first_l = col_ceil(P, c.lo_tok);
+    const int last_l = min(col_floor(P, c.lo_tok + deg - 1), P.VL - 1);
+    const bool dense_window = c.dense && !processed_div && first_l <= last_l && first_l >= c.wlo && last_l <= c.whi;
+    const int wn = last_l - c.wlo + 1;              // window entries up to the last local child
+    const int jb = P.voff + c.wlo * vs - c.lo_tok;  // child index of window entry 0
+    const int nloc = last_l - first_l + 1;          // local children
+    const int d0 = first_l - c.wlo;                 // window index of the first local child
     static_assert(kBatch == kThreads * 8, "dense path: one 8-entry group per thread per batch");
     bool dense_done = false;
     constexpr int kG = 4;   // the one-pass dense scan covers kG * kBatch window entries
     // an EOS child scores -inf in the pool: the value bound then takes one child more
     const int eos_j = (P.eos >= 0) ? P.eos - c.lo_tok : -1;
-    const int ksel = P.k2 + ((eos_j >= 0 && eos_j < deg) ? 1 : 0);
-    for (int attempt = 0; attempt < 2 && !dense_done && dense_window && d0 + deg <= kG * kBatch; ++attempt) {
-      if ((S.v->thr_key == 0ull || attempt == 1) && deg > ksel) {
+    const int eos_l = (eos_j >= 0 && eos_j < deg) ? col_of(P, P.eos) : -1;   // its local column
+    const int eos_w = (eos_l >= 0) ? eos_l - c.wlo : -1;                       // and window entry
+    const int ksel = P.k2 + (eos_l >= 0 ? 1 : 0);
+    for (int attempt = 0; attempt < 2 && !dense_done && dense_window && wn <= kG * kBatch; ++attempt) {
+      if ((S.v->thr_key == 0ull || attempt == 1) && nloc > ksel) {
         // a weak bound: tighten it with the row's own 2B-th best child value
         // (the (2B+1)-th when one child is EOS).  Scores are monotone in the
         // value, so every child scoring at least that value's score is kept,
         // and at least 2B children other than EOS do.
-        const Cut vc = cta_radix_select([this, d0](int j) { return win_value_key(d0 + j, j); }, deg, ksel, S.sel);
+        const Cut vc = cta_radix_select([this, d0](int q) { return win_value_key(d0 + q, q); }, nloc, ksel, S.sel);
         if (threadIdx.x == 0) {
           const float xt = value_of_key(vc.floor_key());
           const float st = __fadd_rn(__fadd_rn(c.cum, __fsub_rn(xt, lse)), 0.0f);
@@ -644,8 +678,7 @@ struct Step {
       for (int g = 0; g < kG; ++g) {
         pm[g] = 0;
         const int w0 = g * kBatch + static_cast<int>(threadIdx.x) * 8;
-        const int i0 = w0 - d0;
-        if (w0 < d0 + deg) {
+        if (w0 < wn) {
           float x[8];
           win_load8(w0, x);
           float xm = x[0];
@@ -653,11 +686,11 @@ struct Step {
           for (int i = 1; i < 8; ++i) xm = fmaxf(xm, x[i]);
           // scores are monotone in the value: a group whose best score misses the
           // bound has no candidate (only its EOS child, if any, needs a look)
-          const bool eos_here = eos_j >= i0 && eos_j < i0 + 8;
+          const bool eos_here = eos_w >= w0 && eos_w < w0 + 8;
           if (eos_here || !(__fadd_rn(c.cum, __fsub_rn(xm, lse)) < thr_s)) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              const int j = i0 + i;
+              const int j = jb + (w0 + i) * vs;
               const bool in = (j >= 0) && (j < deg);
               float sc = __fadd_rn(c.cum, __fsub_rn(x[i], lse));
               if (in && j == eos_j) {
@@ -675,13 +708,12 @@ struct Step {
       for (int g = 0; g < kG; ++g) {
         if (pm[g]) {
           const int w0 = g * kBatch + static_cast<int>(threadIdx.x) * 8;
-          const int i0 = w0 - d0;
           float x[8];
           win_load8(w0, x);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             if ((pm[g] >> i) & 1u) {
-              const int j = i0 + i;
+              const int j = jb + (w0 + i) * vs;
               const float sc = (j == eos_j) ? -kInf : __fadd_rn(c.cum, __fsub_rn(x[i], lse));
               if (pos < static_cast<uint32_t>(kKeyCap))
                 S.keys[pos] = make_key(sc, fb + static_cast<uint32_t>(j));
@@ -707,24 +739,25 @@ struct Step {
     if (dense_done) {
       // every child was scored in the one pass
     } else if (dense_window) {
-      // child j sits at window index d0 + j: 8 window entries per thread per 16-byte load
-      for (int base = 0; base < d0 + deg; base += kBatch) {
+      // 8 window entries per thread per 16-byte load; entry w holds child jb + w * vs
+      for (int base = 0; base < wn; base += kBatch) {
         const uint64_t thr = S.v->thr_key;
         const float thr_s = thr ? key_score(thr) : -kInf;
         // other rows of the request raise its bound meanwhile: read it for the next batch
         uint64_t tau_g = 0;
-        if (threadIdx.x == 0 && base + kBatch < d0 + deg) tau_g = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
+        if (threadIdx.x == 0 && base + kBatch < wn) tau_g = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
         const int w0 = base + static_cast<int>(threadIdx.x) * 8;   // kBatch == kThreads * 8
-        const int i0 = w0 - d0;                                     // child index of entry w0
+        const int j0 = jb + w0 * vs;                                // child index of entry w0
         float x[8];
         bool p[8];
         bool any = false;
-        if (w0 < d0 + deg) {
+        if (w0 < wn) {
           win_load8(w0, x);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float sc = __fadd_rn(c.cum, __fsub_rn(x[i], lse));
-            p[i] = (i0 + i >= 0) && (i0 + i < deg) && (sc >= thr_s || c.lo_tok + i0 + i == P.eos);
+            const int j = j0 + i * vs;
+            p[i] = (j >= 0) && (j < deg) && (sc >= thr_s || c.lo_tok + j == P.eos);
             any |= p[i];
           }
         } else {
@@ -738,7 +771,7 @@ struct Step {
           for (int i = 0; i < 8; ++i) {
             kv[i] = 0;
             if (p[i]) {
-              kv[i] = child_key(c, c.lo_tok + i0 + i, i0 + i, x[i], lse, fb);
+              kv[i] = child_key(c, c.lo_tok + j0 + i * vs, j0 + i * vs, x[i], lse, fb);
               if (kv[i] >= thr) mask |= 1u << i;
             }
           }
@@ -746,7 +779,7 @@ struct Step {
         }
         if (threadIdx.x == 0 && tau_g > S.v->thr_key) S.v->thr_key = tau_g;
         csync();
-        if (base + kBatch < d0 + deg && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
+        if (base + kBatch < wn && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
           const Cut cut = shrink_to(P.k2);
           raise_tau(c.r, cut.floor_key());
         }
@@ -780,8 +813,8 @@ struct Step {
             if (tok >= P.V) {
               atomicOr(P.err, GR_DEVERR_BAD_CHILD);
             } else {
-              const int tl = tok - P.voff;
-              if (tl >= 0 && tl < P.VL) {
+              const int tl = col_of(P, tok);
+              if (tl >= 0) {
                 const float x = (tl >= c.wlo && tl <= c.whi) ? win_load(tl - c.wlo) : load_logit(c, tl);
                 xs[i] = x;
                 const float y = exact_y(c, x, tl);
@@ -862,7 +895,7 @@ struct Step {
     // columns per thread per batch: a batch must fit beside the k kept keys
     const int per = max(1, min(kMaxPer, (kKeyCap - k) / kThreads));
     const int nb = per * kThreads;
-    const uint32_t fb = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V) + static_cast<uint32_t>(P.voff);
+    const uint32_t fb = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V);
     uint64_t thr = 0ull;
     for (int base = 0; base < P.VL; base += nb) {
       uint64_t kv[kMaxPer];
@@ -874,8 +907,9 @@ struct Step {
         if (i < per && tl < P.VL) {
           const float lp = __fsub_rn(exact_y(c, load_logit(c, tl), tl), lse);
           float sc = lp_only ? lp : __fadd_rn(c.cum, lp);
-          if (!lp_only && P.voff + tl == P.eos) sc = -kInf;
-          kv[i] = make_key(sc, fb + static_cast<uint32_t>(tl));
+          const int tok = tok_of(P, tl);
+          if (!lp_only && tok == P.eos) sc = -kInf;
+          kv[i] = make_key(sc, fb + static_cast<uint32_t>(tok));
           if (kv[i] >= thr) mask |= 1u << i;
         }
       }
@@ -910,8 +944,9 @@ struct Step {
       if (tok == P.eos) sc = -kInf;
       S.keys[i] = make_key(sc, flat);
     }
-    if (threadIdx.x == 0 && P.eos >= P.voff && P.eos < P.voff + P.VL && P.eos_score) {
-      const int tl = P.eos - P.voff;
+    const int eos_l = (P.eos >= 0) ? col_of(P, P.eos) : -1;
+    if (threadIdx.x == 0 && eos_l >= 0 && P.eos_score) {
+      const int tl = eos_l;
       const float y = exact_y(c, load_logit(c, tl), tl);
       P.eos_score[c.row] = __fadd_rn(c.cum, __fsub_rn(y, lse));
     }
@@ -949,7 +984,7 @@ struct Step {
       const int n = min(static_cast<int>(S.v->cnt), kKeyCap);
       uint64_t best = 0;
       for (int i = threadIdx.x; i < n; i += kThreads) {
-        const int tl = static_cast<int>(key_flat(S.keys[i]) - vb) - P.voff;
+        const int tl = col_of(P, static_cast<int>(key_flat(S.keys[i]) - vb));
         if (flagged(c, tl)) continue;
         const uint64_t k = make_key(load_logit(c, tl), static_cast<uint32_t>(tl));
         best = k > best ? k : best;
@@ -993,7 +1028,7 @@ struct Step {
     }
     // dedup against the sampled token (vllm_gr/logprobs.py:47-52)
     if (sampled_tl >= 0) {
-      const uint32_t sflat = vb + static_cast<uint32_t>(P.voff + sampled_tl);
+      const uint32_t sflat = vb + static_cast<uint32_t>(tok_of(P, sampled_tl));
       if (threadIdx.x == 0) S.v->last = 0;
       csync();
       for (int i = threadIdx.x; i < n; i += kThreads)
@@ -1142,8 +1177,8 @@ __device__ __forceinline__ void fill_row_ctx(const Params& P, const int* rec, Ro
     const int lt = rec[kMLo], ht = rec[kMHi];
     c.lo_tok = lt;
     c.dense = (ht - lt + 1) == (c.c1 - c.c0);
-    const int lo = max(lt - P.voff, 0);
-    const int hi = min(ht - P.voff, P.VL - 1);
+    const int lo = col_ceil(P, lt);
+    const int hi = min(col_floor(P, ht), P.VL - 1);
     if (lo <= hi) {
       c.wlo = lo & ~7;                 // window index 0 = an 8-aligned column
       c.whi = min(hi, c.wlo + Step<TL>::kWinTok - 1);
@@ -1410,8 +1445,8 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
       const int* h = P.hist + static_cast<size_t>(c.row) * P.T;
       for (int t = tid; t < P.T; t += kThreads) {
         const int tok = h[t];
-        const int tl = tok - P.voff;
-        if (tok >= 0 && tl >= 0 && tl < P.VL) {
+        const int tl = (tok >= 0) ? col_of(P, tok) : -1;
+        if (tl >= 0) {
           const uint32_t bit = 1u << (tl & 31);
           const uint32_t old = atomicOr(&S.bitmap[tl >> 5], bit);
           if (!(old & bit)) {
@@ -1676,7 +1711,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
           if (cl) {
             const unsigned char* stage_p = S.ring + static_cast<size_t>(cstage) * kStageBytes;
             const uint32_t fbase = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V) +
-                                   static_cast<uint32_t>(P.voff + tbase);
+                                   static_cast<uint32_t>(tok_of(P, tbase));
             uint32_t pos = base + inc - cl;
             uint32_t mk = pm;
             while (mk) {
@@ -1685,7 +1720,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
               const int col = (tid + (e / EPV) * kThreads) * EPV + (e % EPV);
               const float x = Tr::load_s(stage_p, col);
               const float ye = (P.mode == kModeProcessed && c.teff != 1.0f) ? __fdiv_rn(x, c.teff) : x;
-              S.keys[pos++] = make_key(ye, fbase + static_cast<uint32_t>(col));
+              S.keys[pos++] = make_key(ye, fbase + static_cast<uint32_t>(col * P.vstride));
             }
           }
           cnt_prev = cnt_now;
@@ -1783,7 +1818,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
           uint64_t key = 0;
           if (valid) {
             key = make_key(y[0], static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V) +
-                                     static_cast<uint32_t>(P.voff + S.tab_tok[j]));
+                                     static_cast<uint32_t>(tok_of(P, S.tab_tok[j])));
             pred = key >= thr_key;
           }
           warp_append(pred, key, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
@@ -2272,8 +2307,10 @@ static size_t ws_meta_bytes(int R, int NB) { return align128(size_t(R) * NB * kM
 static int validate(const gr_step_desc* d) {
   if (!d) return GR_ERR_NULL;
   if (d->num_requests < 1 || d->num_beams < 1 || d->beam_width < 1) return GR_ERR_BAD_DESC;
-  if (d->vocab_size < 1 || d->vocab_local < 1 || d->vocab_offset < 0) return GR_ERR_BAD_DESC;
-  if (static_cast<long long>(d->vocab_offset) + d->vocab_local > d->vocab_size) return GR_ERR_BAD_DESC;
+  if (d->vocab_size < 1 || d->vocab_local < 1 || d->vocab_offset < 0 || d->vocab_stride < 0) return GR_ERR_BAD_DESC;
+  // the last local column's token: vocab_offset + (vocab_local - 1) * stride < vocab_size
+  const long long vstride = d->vocab_stride > 1 ? d->vocab_stride : 1;
+  if (static_cast<long long>(d->vocab_offset) + (d->vocab_local - 1) * vstride >= d->vocab_size) return GR_ERR_BAD_DESC;
   if (d->row_stride < d->vocab_local) return GR_ERR_BAD_DESC;
   if (d->logit_dtype < GR_DTYPE_F32 || d->logit_dtype > GR_DTYPE_F16) return GR_ERR_DTYPE;
   if (d->logprobs_mode != GR_LOGPROBS_RAW && d->logprobs_mode != GR_LOGPROBS_PROCESSED) return GR_ERR_DTYPE;
@@ -2310,6 +2347,7 @@ static void fill_params(Params& P, const gr_step_desc* d, const gr_step_io* io) 
   P.V = d->vocab_size;
   P.VL = d->vocab_local;
   P.voff = d->vocab_offset;
+  P.vstride = d->vocab_stride > 1 ? d->vocab_stride : 1;
   P.row_stride = d->row_stride;
   P.mode = d->logprobs_mode;
   P.K = d->per_beam_k;

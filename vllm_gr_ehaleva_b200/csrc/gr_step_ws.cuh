@@ -187,7 +187,7 @@ __device__ void ws_produce(const Params& P) {
       int wlo = 1, whi = 0;
       uint32_t wbytes = 0;
       if (P.K == 0 && !P.partial_only && !P.stall_copies && node >= 0 && c1 > c0) {
-        const int lo = max(lt - P.voff, 0), hi = min(ht - P.voff, P.VL - 1);
+        const int lo = col_ceil(P, lt), hi = min(col_floor(P, ht), P.VL - 1);
         if (lo <= hi) {
           const uintptr_t body0 = (a + 15) & ~uintptr_t(15);
           const uintptr_t body1 = (a + static_cast<uintptr_t>(P.VL) * ES) & ~uintptr_t(15);

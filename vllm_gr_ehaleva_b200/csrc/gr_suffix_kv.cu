@@ -377,6 +377,10 @@ extern "C" int32_t gr_suffix_records(int32_t num_reqs, const int64_t* q_starts, 
     const int64_t room = q_len - own0, full = (w - 1) * st;
     const int64_t extra = room < full ? room : full;
     const int64_t beams = 1 + (extra + st - 1) / st;
+    // the records' 32-bit fields must hold these (no silent wrap for large inputs)
+    constexpr int64_t kI32Max = 0x7FFFFFFF;
+    if (remaining > kI32Max || own0 + extra > kI32Max || beams > kI32Max || beam_base + beams > kI32Max)
+      return GR_ERR_BAD_DESC;
     gr_suffix_req& r = recs[n++];
     r.q_start = q_start;
     r.out_base = out_base;

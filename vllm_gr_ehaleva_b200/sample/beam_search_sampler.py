@@ -83,10 +83,10 @@ class Workspace:
         return self.buf
 
 
-def make_desc(*, R, NB, B, V, VL, voff, row_stride, dtype, mode, K, eos, T, N, E) -> _lib.StepDesc:
+def make_desc(*, R, NB, B, V, VL, voff, row_stride, dtype, mode, K, eos, T, N, E, VS=1) -> _lib.StepDesc:
     d = _lib.StepDesc()
     d.num_requests, d.num_beams, d.beam_width = R, NB, B
-    d.vocab_size, d.vocab_local, d.vocab_offset = V, VL, voff
+    d.vocab_size, d.vocab_local, d.vocab_offset, d.vocab_stride = V, VL, voff, VS
     d.row_stride = row_stride
     d.logit_dtype, d.logprobs_mode, d.per_beam_k = dtype, mode, K
     d.eos_token_id, d.hist_len, d.num_nodes, d.num_edges = eos, T, N, E
@@ -105,8 +105,9 @@ def _prepare(logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor, *, bea
              logprobs_mode: str = "raw_logprobs", per_beam_k: int = 0, eos_token_id: Optional[int] = None,
              hist: Optional[torch.Tensor] = None, temperature=None, repetition_penalty=None,
              presence_penalty=None, frequency_penalty=None, workspace: Optional[Workspace] = None,
-             stream: Optional[torch.cuda.Stream] = None):
-    """Checks the step inputs and builds (descriptor, io, outputs, workspace, stream)."""
+             stream: Optional[torch.cuda.Stream] = None, vocab_stride: int = 1):
+    """Checks the step inputs and builds (descriptor, io, outputs, workspace, stream).
+    Local logit column j holds token vocab_offset + j * vocab_stride."""
     if not logits.is_cuda:
         raise ValueError("logits must be a CUDA tensor")
     device = logits.device
@@ -150,7 +151,8 @@ def _prepare(logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor, *, bea
     mode = LOGPROBS_MODES[logprobs_mode]
     eos = -1 if eos_token_id is None else int(eos_token_id)
     desc = make_desc(R=R, NB=NB, B=B, V=V, VL=VL, voff=int(vocab_offset), row_stride=int(row_stride),
-                     dtype=_DTYPES[logits.dtype], mode=mode, K=int(per_beam_k), eos=eos, T=T, N=N, E=E)
+                     dtype=_DTYPES[logits.dtype], mode=mode, K=int(per_beam_k), eos=eos, T=T, N=N, E=E,
+                     VS=int(vocab_stride))
     temps = _per_request(temperature, R, device)
     reps = _per_request(repetition_penalty, R, device)
     press = _per_request(presence_penalty, R, device)

@@ -83,15 +83,19 @@ def merge_candidates(local_logits: torch.Tensor, cum: torch.Tensor, node: torch.
 
 def sharded_beam_step(local_logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor, *,
                       all_gather: Callable[[torch.Tensor], torch.Tensor], beam_width: int, vocab_size: int,
-                      vocab_offset: int, csr=None, eos_token_id: Optional[int] = None,
+                      vocab_offset: int, vocab_stride: int = 1, csr=None, eos_token_id: Optional[int] = None,
                       hist: Optional[torch.Tensor] = None, logprobs_mode: str = "raw_logprobs",
                       temperature=None, repetition_penalty=None, presence_penalty=None, frequency_penalty=None,
                       workspace: Optional[Workspace] = None,
                       stream: Optional[torch.cuda.Stream] = None) -> BeamStepOutput:
     """One constrained beam step over vocabulary-sharded logits; every rank
-    returns the same outputs.  eos_score comes from the rank whose columns hold
-    the EOS token (NaN elsewhere, so the first non-NaN over ranks is taken)."""
+    returns the same outputs.  Local column j holds token vocab_offset +
+    j * vocab_stride (a contiguous slice, or shard k = vocab_offset of a
+    strided split over vocab_stride ranks).  eos_score comes from the rank
+    whose columns hold the EOS token (NaN elsewhere, so the first non-NaN over
+    ranks is taken)."""
     kw = dict(beam_width=beam_width, csr=csr, vocab_size=vocab_size, vocab_offset=vocab_offset,
+              vocab_stride=vocab_stride,
               logprobs_mode=logprobs_mode, per_beam_k=0, eos_token_id=eos_token_id, hist=hist,
               temperature=temperature, repetition_penalty=repetition_penalty, presence_penalty=presence_penalty,
               frequency_penalty=frequency_penalty, workspace=workspace, stream=stream)
@@ -139,7 +143,8 @@ class ShardedStepper:
     be its inputs) and are overwritten by the step after that."""
 
     def __init__(self, *, num_requests: int, num_beams: int, beam_width: int, vocab_size: int, vocab_local: int,
-                 vocab_offset: int, num_shards: int, csr, hist_len: int, logits_dtype=torch.bfloat16,
+                 vocab_offset: int, num_shards: int, csr, hist_len: int, vocab_stride: int = 1,
+                 logits_dtype=torch.bfloat16,
                  row_stride: Optional[int] = None, eos_token_id: Optional[int] = None,
                  all_gather: Optional[Callable[[torch.Tensor], torch.Tensor]] = None, group=None, device=None):
         from .sample.beam_search_sampler import _DTYPES, make_desc, workspace_size
@@ -154,7 +159,7 @@ class ShardedStepper:
                               row_stride=int(row_stride if row_stride is not None else vocab_local),
                               dtype=_DTYPES[logits_dtype], mode=_lib.LOGPROBS_RAW, K=0,
                               eos=-1 if eos_token_id is None else int(eos_token_id), T=self.T,
-                              N=int(row_ptr.numel()) - 1, E=int(child_tok.numel()))
+                              N=int(row_ptr.numel()) - 1, E=int(child_tok.numel()), VS=int(vocab_stride))
         dev = dict(device=self.device)
         f32, i32 = dict(dtype=torch.float32, **dev), dict(dtype=torch.int32, **dev)
         self.outs = [BeamStepOutput(
@@ -182,7 +187,13 @@ class ShardedStepper:
         dist.all_gather_into_tensor(dst, src, group=self.group)
 
     def step(self, local_logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor,
-             hist: Optional[torch.Tensor] = None) -> BeamStepOutput:
+             hist: Optional[torch.Tensor] = None, marks: Optional[list] = None) -> BeamStepOutput:
+        """One step.  `marks`: six CUDA events to record on the current stream
+        around the phases (start, lse partials, their all-gather, shard
+        candidates, their all-gather, merge), for timing them apart."""
+        def mark(i):
+            if marks is not None:
+                marks[i].record()
         out = self.outs[self.k & 1]
         self.k += 1
         io = _lib.StepIO()
@@ -198,13 +209,19 @@ class ShardedStepper:
         s = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
         d, iop = ctypes.byref(self.desc), ctypes.byref(io)
         wsp, wsn = ctypes.c_void_p(self.ws.data_ptr()), ctypes.c_size_t(self.ws.numel())
+        mark(0)
         _lib.check(self.lib.gr_lse_partials(d, iop, vp(self.partials), wsp, wsn, s), "gr_lse_partials")
+        mark(1)
         self._gather(self.gathered_p, self.partials)
+        mark(2)
         _lib.check(self.lib.gr_shard_candidates(d, iop, vp(self.gathered_p), ctypes.c_int32(self.S), vp(self.keys),
                                                 wsp, wsn, s), "gr_shard_candidates")
+        mark(3)
         self._gather(self.gathered_k, self.keys)
+        mark(4)
         _lib.check(self.lib.gr_merge_candidates(d, iop, vp(self.gathered_k), ctypes.c_int32(self.S), wsp, wsn, s),
                    "gr_merge_candidates")
+        mark(5)
         if self.eos is not None:
             self._gather(self.eos_all, out.eos_score)
             eos = self.eos_all[0]
