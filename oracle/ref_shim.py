@@ -22,9 +22,12 @@ those names (everything else resolves to the installed vLLM):
 
 The mock engine restates vLLM's sampler for a beam: float32 logits of the
 beam's full token sequence (content addressed, so the reference's unordered
-beam order cannot change its inputs), lp = log_softmax(logits), the top-K
-list [sampled, top1..topK] with the greedy token as `sampled`
-(vllm v1/sample/sampler.py:300-352).  In "allowed" mode the top-K list holds
+beam order cannot change its inputs; optionally rounded to bf16 values, as a
+bf16 model's logits are), lp = log_softmax(logits) -- or, with vLLM's
+logprobs_mode "processed_logprobs", log_softmax(logits / T) with the
+temperature the reference's loop put in its SamplingParams (T < 1e-5 counts
+as 1) -- and the top-K list [sampled, top1..topK] with the greedy token as
+`sampled` (vllm v1/sample/sampler.py:223-233, 300-352).  In "allowed" mode the top-K list holds
 the beam's best K catalog children (so the reference's own mask/add/EOS/select
 code yields the constrained result); in "raw" mode it is the plain top-K and the
 reference masks it itself (serving_engine.py:504-506).
@@ -235,16 +238,20 @@ class MockEngine:
     """Engine client for serving_engine.beam_search (ADD_BATCH path) and an LLM
     stand-in for llm.beam_search: every request is one beam advancing one token."""
 
-    def __init__(self, vocab, sigma, seed, bf16, prompt_len_of: Callable | None = None, allowed_fn=None):
+    def __init__(self, vocab, sigma, seed, bf16, prompt_len_of: Callable | None = None, allowed_fn=None,
+                 processed: bool = False):
         self.vocab, self.sigma, self.seed, self.bf16 = vocab, sigma, seed, bf16
+        self.processed = processed            # vLLM logprobs_mode "processed_logprobs"
         self.allowed_fn = allowed_fn          # tokens -> allowed child ids (or None = raw top-K)
         self.calls: list[list[list[int]]] = []  # beams requested per step
         self._pending: dict = {}
 
-    def output_for(self, tokens, k):
+    def output_for(self, tokens, k, temperature=None):
         from vllm.logprobs import FlatLogprobs
         from vllm.outputs import CompletionOutput
         x = beam_logits(tokens, self.vocab, self.sigma, self.seed, self.bf16)
+        if self.processed and temperature is not None and temperature >= 1e-5:
+            x = (x / np.float32(temperature)).astype(np.float32)
         lp = log_softmax32(x)
         allowed = None if self.allowed_fn is None else self.allowed_fn(tokens)
         top = top_list(lp, k, allowed)
@@ -264,19 +271,21 @@ class MockEngine:
     def prepare_request(self, request_id, prompt, params, **kwargs):
         q = asyncio.Queue()
         req = types.SimpleNamespace(request_id=request_id, tokens=list(prompt["prompt_token_ids"]),
-                                    k=params.logprobs, queue=q, metrics=None)
+                                    k=params.logprobs, temperature=params.temperature, queue=q, metrics=None)
         return q, req
 
     async def _add_requests_batch(self, reqs, use_batch_message=False):
         self.calls.append([list(r.tokens) for r in reqs])
         for r in reqs:
-            out = types.SimpleNamespace(outputs=[self.output_for(r.tokens, r.k)], finished=True, metrics=None)
+            out = types.SimpleNamespace(outputs=[self.output_for(r.tokens, r.k, r.temperature)], finished=True,
+                                        metrics=None)
             await r.queue.put(out)
 
     # ---- LLM stand-in (offline) ----
     def generate(self, prompts, sampling_params=None, use_tqdm=False, lora_request=None):
         self.calls.append([list(p["prompt_token_ids"]) for p in prompts])
-        return [types.SimpleNamespace(outputs=[self.output_for(list(p["prompt_token_ids"]), sampling_params.logprobs)])
+        return [types.SimpleNamespace(outputs=[self.output_for(list(p["prompt_token_ids"]), sampling_params.logprobs,
+                                                               sampling_params.temperature)])
                 for p in prompts]
 
 
@@ -299,7 +308,7 @@ class Tok:
 
 
 def run_online(reference_root, prompt_tokens, *, beam_width, max_tokens, vocab, sigma, seed, bf16, catalog_seqs,
-               begin_token, end_token, eos_token_id, ignore_eos, mode):
+               begin_token, end_token, eos_token_id, ignore_eos, mode, processed=False, temperature=0.0):
     """serving_engine.beam_search with a catalog; returns (calls, final beams)."""
     install(reference_root)
     from vllm_gr.entrypoints.openai import serving_engine
@@ -317,10 +326,11 @@ def run_online(reference_root, prompt_tokens, *, beam_width, max_tokens, vocab, 
     allowed_fn = None
     if mode == "allowed":
         allowed_fn = lambda toks: np.array(sorted(cat.valid(toks[plen:])), dtype=np.int64)  # noqa: E731
-    eng = MockEngine(vocab, sigma, seed, bf16, allowed_fn=allowed_fn)
+    eng = MockEngine(vocab, sigma, seed, bf16, allowed_fn=allowed_fn, processed=processed)
     this = types.SimpleNamespace(engine_client=eng, input_processor=types.SimpleNamespace(tokenizer=tok),
                                  models=types.SimpleNamespace(catalog=cat))
-    params = BeamSearchParams(beam_width=beam_width, max_tokens=max_tokens, ignore_eos=ignore_eos, temperature=0.0,
+    params = BeamSearchParams(beam_width=beam_width, max_tokens=max_tokens, ignore_eos=ignore_eos,
+                              temperature=temperature,
                               begin_token=None if begin_token is None else str(begin_token),
                               end_token=None if end_token is None else str(end_token))
 
@@ -336,17 +346,17 @@ def run_online(reference_root, prompt_tokens, *, beam_width, max_tokens, vocab, 
 
 
 def run_offline(reference_root, prompts, *, beam_width, max_tokens, vocab, sigma, seed, bf16, eos_token_id,
-                ignore_eos, length_penalty):
+                ignore_eos, length_penalty, processed=False, temperature=0.0):
     """llm.beam_search (no catalog); returns (calls, final beams per prompt)."""
     install(reference_root)
     from vllm_gr.entrypoints import llm as llm_mod
     from vllm_gr.sampling_params import BeamSearchParams
 
     tok = Tok(eos_token_id)
-    eng = MockEngine(vocab, sigma, seed, bf16)
+    eng = MockEngine(vocab, sigma, seed, bf16, processed=processed)
     this = types.SimpleNamespace(_get_beam_search_lora_requests=lambda lr, ps: [None] * len(ps),
                                  get_tokenizer=lambda: tok, generate=eng.generate)
-    params = BeamSearchParams(beam_width=beam_width, max_tokens=max_tokens, ignore_eos=ignore_eos, temperature=0.0,
-                              length_penalty=length_penalty)
+    params = BeamSearchParams(beam_width=beam_width, max_tokens=max_tokens, ignore_eos=ignore_eos,
+                              temperature=temperature, length_penalty=length_penalty)
     outs = llm_mod.beam_search(this, [{"prompt_token_ids": list(p)} for p in prompts], params)
     return eng.calls, [[(list(s.tokens), float(s.cum_logprob), s.finish_reason) for s in o.sequences] for o in outs]

@@ -42,9 +42,12 @@ class _Instance:
     completed: list = field(default_factory=list)
 
 
-def device_step_fn(device="cuda", csr: Optional[CSRTrie] = None, dtype="f32", per_beam_k: int = 0):
+def device_step_fn(device="cuda", csr: Optional[CSRTrie] = None, dtype="f32", per_beam_k: int = 0,
+                   logprobs_mode: str = "raw_logprobs", temperature: Optional[float] = None):
     """step_fn running the CUDA step; logits are copied to the device per call.
-    per_beam_k = beam width gives llm.py's per-beam top-K candidate lists."""
+    per_beam_k = beam width gives llm.py's per-beam top-K candidate lists;
+    logprobs_mode / temperature are vLLM's (the temperature of the requests'
+    SamplingParams, used by the processed mode)."""
     import torch
 
     from .sample import beam_step
@@ -57,7 +60,9 @@ def device_step_fn(device="cuda", csr: Optional[CSRTrie] = None, dtype="f32", pe
         x = torch.from_numpy(np.ascontiguousarray(logits32)).to(device).to(tdt)
         out = beam_step(x, torch.from_numpy(cum).to(device), torch.from_numpy(node).to(device),
                         beam_width=beam_width, csr=csr_dev, vocab_size=vocab_size, per_beam_k=per_beam_k,
-                        eos_token_id=None if eos_token_id is None or eos_token_id < 0 else eos_token_id)
+                        eos_token_id=None if eos_token_id is None or eos_token_id < 0 else eos_token_id,
+                        logprobs_mode=logprobs_mode,
+                        temperature=None if temperature is None else [temperature] * cum.shape[0])
         out.check()
         return {k: getattr(out, k).cpu().numpy() for k in ("sel_token", "sel_parent", "sel_score", "sel_node",
                                                           "eos_score")}
