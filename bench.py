@@ -320,17 +320,18 @@ def run_ours(args):
     # algorithmic bytes of one cycle of levels (host-side, outside timing)
     bytes_cycle = []
     run_chain(levels, bytes_acc=bytes_cycle)
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    clocks = ClockSampler(device.index if world == 1 else local)
+    clocks.start()
+    time.sleep(0.5)          # let nvidia-smi start sampling before the timed region
+    # the warm-up steps run right before the timed ones (after the pause above,
+    # so that the GPU is out of its idle state when the timing starts)
     out = run_chain(max(args.warmup, 3))
     torch.cuda.synchronize()
     err = int(out.err.item())
-
-    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    clocks = ClockSampler(device.index if world == 1 else local)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks.start()
-    time.sleep(0.5)          # let nvidia-smi start sampling before the timed region
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
@@ -682,14 +683,14 @@ def run_sharded(args):
                 cum, node, hist = out.sel_score, out.sel_node, out.hist_out
         return out
 
-    out = chain(max(args.warmup, 3))
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    out = chain(max(args.warmup, 3))          # warm-up right before the timed steps
     torch.cuda.synchronize()
     err = int(out.err.item())
     dist.barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)

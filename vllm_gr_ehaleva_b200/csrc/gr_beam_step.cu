@@ -630,33 +630,25 @@ struct Step {
     // first; only the (rare) passers build keys and take part in the append.
     // An exact float test is enough: key >= thr implies score >= score(thr).
     const bool processed_div = (P.mode == kModeProcessed) && (c.excl || c.teff != 1.0f);
-    // A dense node's children are the tokens lo_tok .. lo_tok + deg - 1; this
-    // shard holds those in local columns first_l .. last_l.  Window entry w is
-    // local column wlo + w, the child of index jb + w * vs (outside [0, deg):
-    // not a child).
-    const int vs = P.vstride;
-    const int first_l = col_ceil(P, c.lo_tok);
-    const int last_l = min(col_floor(P, c.lo_tok + deg - 1), P.VL - 1);
-    const bool dense_window = c.dense && !processed_div && first_l <= last_l && first_l >= c.wlo && last_l <= c.whi;
-    const int wn = last_l - c.wlo + 1;              // window entries up to the last local child
-    const int jb = P.voff + c.wlo * vs - c.lo_tok;  // child index of window entry 0
-    const int nloc = last_l - first_l + 1;          // local children
-    const int d0 = first_l - c.wlo;                 // window index of the first local child
+    // the window path: a contiguous shard holding every child of a dense node
+    // in its child window, child j at window entry d0 + j
+    const int first = c.lo_tok - P.voff;
+    const bool dense_window = P.vstride == 1 && c.dense && !processed_div && first >= c.wlo &&
+                              first + deg - 1 <= c.whi;
+    const int d0 = first - c.wlo;               // window index of the first child
     static_assert(kBatch == kThreads * 8, "dense path: one 8-entry group per thread per batch");
     bool dense_done = false;
     constexpr int kG = 4;   // the one-pass dense scan covers kG * kBatch window entries
     // an EOS child scores -inf in the pool: the value bound then takes one child more
     const int eos_j = (P.eos >= 0) ? P.eos - c.lo_tok : -1;
-    const int eos_l = (eos_j >= 0 && eos_j < deg) ? col_of(P, P.eos) : -1;   // its local column
-    const int eos_w = (eos_l >= 0) ? eos_l - c.wlo : -1;                       // and window entry
-    const int ksel = P.k2 + (eos_l >= 0 ? 1 : 0);
-    for (int attempt = 0; attempt < 2 && !dense_done && dense_window && wn <= kG * kBatch; ++attempt) {
-      if ((S.v->thr_key == 0ull || attempt == 1) && nloc > ksel) {
+    const int ksel = P.k2 + ((eos_j >= 0 && eos_j < deg) ? 1 : 0);
+    for (int attempt = 0; attempt < 2 && !dense_done && dense_window && d0 + deg <= kG * kBatch; ++attempt) {
+      if ((S.v->thr_key == 0ull || attempt == 1) && deg > ksel) {
         // a weak bound: tighten it with the row's own 2B-th best child value
         // (the (2B+1)-th when one child is EOS).  Scores are monotone in the
         // value, so every child scoring at least that value's score is kept,
         // and at least 2B children other than EOS do.
-        const Cut vc = cta_radix_select([this, d0](int q) { return win_value_key(d0 + q, q); }, nloc, ksel, S.sel);
+        const Cut vc = cta_radix_select([this, d0](int j) { return win_value_key(d0 + j, j); }, deg, ksel, S.sel);
         if (threadIdx.x == 0) {
           const float xt = value_of_key(vc.floor_key());
           const float st = __fadd_rn(__fadd_rn(c.cum, __fsub_rn(xt, lse)), 0.0f);
@@ -678,7 +670,8 @@ struct Step {
       for (int g = 0; g < kG; ++g) {
         pm[g] = 0;
         const int w0 = g * kBatch + static_cast<int>(threadIdx.x) * 8;
-        if (w0 < wn) {
+        const int i0 = w0 - d0;
+        if (w0 < d0 + deg) {
           float x[8];
           win_load8(w0, x);
           float xm = x[0];
@@ -686,11 +679,11 @@ struct Step {
           for (int i = 1; i < 8; ++i) xm = fmaxf(xm, x[i]);
           // scores are monotone in the value: a group whose best score misses the
           // bound has no candidate (only its EOS child, if any, needs a look)
-          const bool eos_here = eos_w >= w0 && eos_w < w0 + 8;
+          const bool eos_here = eos_j >= i0 && eos_j < i0 + 8;
           if (eos_here || !(__fadd_rn(c.cum, __fsub_rn(xm, lse)) < thr_s)) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              const int j = jb + (w0 + i) * vs;
+              const int j = i0 + i;
               const bool in = (j >= 0) && (j < deg);
               float sc = __fadd_rn(c.cum, __fsub_rn(x[i], lse));
               if (in && j == eos_j) {
@@ -708,12 +701,13 @@ struct Step {
       for (int g = 0; g < kG; ++g) {
         if (pm[g]) {
           const int w0 = g * kBatch + static_cast<int>(threadIdx.x) * 8;
+          const int i0 = w0 - d0;
           float x[8];
           win_load8(w0, x);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             if ((pm[g] >> i) & 1u) {
-              const int j = jb + (w0 + i) * vs;
+              const int j = i0 + i;
               const float sc = (j == eos_j) ? -kInf : __fadd_rn(c.cum, __fsub_rn(x[i], lse));
               if (pos < static_cast<uint32_t>(kKeyCap))
                 S.keys[pos] = make_key(sc, fb + static_cast<uint32_t>(j));
@@ -739,25 +733,24 @@ struct Step {
     if (dense_done) {
       // every child was scored in the one pass
     } else if (dense_window) {
-      // 8 window entries per thread per 16-byte load; entry w holds child jb + w * vs
-      for (int base = 0; base < wn; base += kBatch) {
+      // child j sits at window index d0 + j: 8 window entries per thread per 16-byte load
+      for (int base = 0; base < d0 + deg; base += kBatch) {
         const uint64_t thr = S.v->thr_key;
         const float thr_s = thr ? key_score(thr) : -kInf;
         // other rows of the request raise its bound meanwhile: read it for the next batch
         uint64_t tau_g = 0;
-        if (threadIdx.x == 0 && base + kBatch < wn) tau_g = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
+        if (threadIdx.x == 0 && base + kBatch < d0 + deg) tau_g = *reinterpret_cast<volatile unsigned long long*>(P.tau + c.r);
         const int w0 = base + static_cast<int>(threadIdx.x) * 8;   // kBatch == kThreads * 8
-        const int j0 = jb + w0 * vs;                                // child index of entry w0
+        const int i0 = w0 - d0;                                     // child index of entry w0
         float x[8];
         bool p[8];
         bool any = false;
-        if (w0 < wn) {
+        if (w0 < d0 + deg) {
           win_load8(w0, x);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float sc = __fadd_rn(c.cum, __fsub_rn(x[i], lse));
-            const int j = j0 + i * vs;
-            p[i] = (j >= 0) && (j < deg) && (sc >= thr_s || c.lo_tok + j == P.eos);
+            p[i] = (i0 + i >= 0) && (i0 + i < deg) && (sc >= thr_s || c.lo_tok + i0 + i == P.eos);
             any |= p[i];
           }
         } else {
@@ -771,7 +764,7 @@ struct Step {
           for (int i = 0; i < 8; ++i) {
             kv[i] = 0;
             if (p[i]) {
-              kv[i] = child_key(c, c.lo_tok + j0 + i * vs, j0 + i * vs, x[i], lse, fb);
+              kv[i] = child_key(c, c.lo_tok + i0 + i, i0 + i, x[i], lse, fb);
               if (kv[i] >= thr) mask |= 1u << i;
             }
           }
@@ -779,7 +772,36 @@ struct Step {
         }
         if (threadIdx.x == 0 && tau_g > S.v->thr_key) S.v->thr_key = tau_g;
         csync();
-        if (base + kBatch < wn && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
+        if (base + kBatch < d0 + deg && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
+          const Cut cut = shrink_to(P.k2);
+          raise_tau(c.r, cut.floor_key());
+        }
+      }
+    } else if (P.vstride > 1 && c.dense) {
+      // a dense node of a strided shard: the shard's children of it sit in
+      // local columns first_l .. last_l (tokens first_l * vstride + voff, ...)
+      const int first_l = col_ceil(P, c.lo_tok);
+      const int nloc = max(0, min(col_floor(P, c.lo_tok + deg - 1), P.VL - 1) - first_l + 1);
+      for (int base = 0; base < nloc; base += kThreads) {
+        const uint64_t thr = S.v->thr_key;
+        const float thr_s = thr ? key_score(thr) : -kInf;
+        const int tl = first_l + base + static_cast<int>(threadIdx.x);
+        const int tok = tok_of(P, tl);
+        bool pass = false;
+        float x = 0.0f;
+        if (base + static_cast<int>(threadIdx.x) < nloc) {
+          x = (tl >= c.wlo && tl <= c.whi) ? win_load(tl - c.wlo) : load_logit(c, tl);
+          pass = (__fadd_rn(c.cum, __fsub_rn(exact_y(c, x, tl), lse)) >= thr_s) || tok == P.eos;
+        }
+        uint64_t kv[1] = {0ull};
+        uint32_t mask = 0;
+        if (pass) {
+          kv[0] = child_key(c, tok, tok - c.lo_tok, x, lse, fb);   // the key carries the child's index
+          if (kv[0] >= thr) mask = 1u;
+        }
+        warp_append_n<1>(mask, kv, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
+        csync();
+        if (base + kThreads < nloc && static_cast<int>(S.v->cnt) > kKeyCap - kThreads) {
           const Cut cut = shrink_to(P.k2);
           raise_tau(c.r, cut.floor_key());
         }
