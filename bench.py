@@ -229,14 +229,19 @@ def initial_state(wl, device):
 
 
 def step_kernel_name(wl) -> str:
-    """The step kernel the library picks for this workload: the warp-specialised
-    one unless GR_BEAM_KERNEL=stream or the step applies penalties in the
-    processed domain (those rows need the penalty table of the streaming kernel)."""
+    """The step kernel the library picks for this workload: the selecting
+    warp-specialised kernel for steps without a catalog, else the
+    warp-specialised one unless GR_BEAM_KERNEL=stream or the step applies
+    penalties in the processed domain."""
     choice = os.environ.get("GR_BEAM_KERNEL", "auto")
     cfg = wl["cfg"]
+    if choice == "stream":
+        return "fused_step_kernel"
+    if wl["catalog"] is None and choice != "ws":
+        return "fused_select_ws_kernel"      # steps without a catalog: every row streamed
     # step_kwargs passes the penalty lists in the processed mode; histories are non-empty
     penalised = cfg["mode"] == "processed"
-    if choice == "stream" or (choice != "ws" and penalised):
+    if choice != "ws" and penalised:
         return "fused_step_kernel"
     return "fused_step_ws_kernel"
 

@@ -24,7 +24,7 @@ from helpers import Case, assert_bit_exact, assert_step_parity, gpu_step, oracle
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True, params=["auto", "stream"])
+@pytest.fixture(autouse=True, params=["auto", "stream", "ws"])
 def step_kernel(request, monkeypatch):
     monkeypatch.setenv("GR_BEAM_KERNEL", request.param)
     return request.param

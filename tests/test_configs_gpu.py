@@ -80,3 +80,24 @@ def test_cfg4_geometry():
         nxt = next_inputs(case, gpu, make_logits(R, B, V, c["sigma"], 401 + step, "f32"))
         nxt.hist = case.hist      # the benchmark's fixed-length penalty history
         case = nxt
+
+
+@pytest.mark.parametrize("dtype,mode", [("f32", "processed_logprobs"), ("bf16", "raw_logprobs")])
+def test_streamed_rows_behind_the_request_bound(dtype, mode):
+    # about 14 rows per SM: most rows start after their request already has a
+    # bound, so in the selecting kernel the streaming warps take their
+    # candidate pass, the finisher warp ends them, and (processed mode) the
+    # penalised columns are masked through the per-row table
+    R, B, V, H = 8, 256, 16384, 64
+    proc = mode == "processed_logprobs"
+    per_req = (lambda v: [v] * R) if proc else (lambda v: None)
+    case = Case(logits32=make_logits(R, B, V, 3.0, 410, dtype), dtype=dtype, cum=initial_cum(R, B),
+                node=np.full((R, B), -1, np.int32), beam_width=B, vocab_size=V,
+                hist=histories(R, B, H, V, seed=5) if proc else None, mode=mode,
+                temperature=per_req(0.7), rep=per_req(1.2), pres=per_req(0.5), freq=per_req(0.1))
+    for step in range(2):
+        gpu = gpu_step(case)
+        assert_step_parity(case, gpu, label=f"many rows {dtype} step {step}")
+        nxt = next_inputs(case, gpu, make_logits(R, B, V, 3.0, 411 + step, dtype))
+        nxt.hist = case.hist      # a fixed penalty history (none in raw mode)
+        case = nxt

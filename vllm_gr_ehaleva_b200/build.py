@@ -18,7 +18,7 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_NAME = "_gr_beam.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 SOURCES = ["gr_beam_step.cu", "gr_suffix_kv.cu", "gr_remux.cu"]
-HEADERS = ["gr_device.cuh", "gr_step_ws.cuh", "gr_nvtx.h"]
+HEADERS = ["gr_device.cuh", "gr_step_ws.cuh", "gr_step_select_ws.cuh", "gr_nvtx.h"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -106,6 +106,9 @@ struct Params {
   unsigned int* rowcnt;        // [R*NB] keys in each row's slot
   int* meta;                   // [R*NB][kMetaWords] row metadata resolved by row_meta_kernel
   unsigned long long* buf;     // [R*NB][2B] per-row candidate slots
+  int* pen_tab;                // [R*NB][2][tabw] each row's penalised local columns, then their processed
+                               // values (bits), valid entries first, -1 after (selecting kernel, or null)
+  int tabw;                    // entries per array: the history length rounded up to 32
   // derived
   int k2;        // 2B candidates
   int kk;        // streamed keep count: max(2B, K) + slack
@@ -323,6 +326,18 @@ __device__ __forceinline__ float penalise(float x, int cnt, float rep, float pre
   return x;
 }
 
+// Lowest y a streamed element needs to reach the request bound tau: its score
+// cum + (y - lse) must reach tau's score, and lse >= L.  -inf without a bound.
+__device__ __forceinline__ float tau_floor_value(uint64_t tau, float cum, float L) {
+  if (tau == 0ull || !(L > -kInf && L < kInf)) return -kInf;
+  const float ts = key_score(tau);
+  const float f = ts - cum + L;
+  if (!(f > -kInf && f < kInf)) return -kInf;
+  // margin for y vs the exact quotient, the approximate logarithms and the
+  // roundings of the score sum (relative to the magnitudes of its terms)
+  return f - 1.0e-5f * (fabsf(f) + fabsf(ts) + fabsf(cum) + fabsf(L)) - 1e-30f;
+}
+
 struct RowCtx {
   int row, r, b, node;
   int c0, c1;          // CSR edge range of the node (c0 == c1: none)
@@ -338,7 +353,9 @@ struct RowCtx {
   float cum;
 };
 
-template <typename TL>
+// kExtTable: the kernel keeps the row's penalty table outside the common
+// shared-memory pieces (and no column bitmap); lookups scan that table.
+template <typename TL, bool kExtTable = false>
 struct Step {
   using Tr = LogitTraits<TL>;
   static constexpr int ES = sizeof(TL);
@@ -347,6 +364,11 @@ struct Step {
   const Params& P;
   int win_off = 0;            // byte offset of the current row's window from the first window
   const int* rec = nullptr;   // the current row's metadata record (shared memory)
+  // kExtTable: the row's penalty table (penalised local columns, their
+  // processed values and count), set per row by the kernel
+  const int* ext_tok = nullptr;
+  const float* ext_y = nullptr;
+  const int* ext_n = nullptr;
   __device__ __forceinline__ explicit Step(const Params& p) : P(p) {}
 
   __device__ __forceinline__ float load_logit(const RowCtx& c, int tl) const {
@@ -378,25 +400,37 @@ struct Step {
   }
 
   __device__ __forceinline__ bool flagged(const RowCtx& c, int tl) const {
-    const Smem S = smem_view(P);
-    return c.pen_active && ((S.bitmap[tl >> 5] >> (tl & 31)) & 1u);
+    if constexpr (kExtTable) {
+      return c.pen_active;
+    } else {
+      const Smem S = smem_view(P);
+      return c.pen_active && ((S.bitmap[tl >> 5] >> (tl & 31)) & 1u);
+    }
   }
 
   __device__ __forceinline__ int table_find(int tl) const {
-    const Smem S = smem_view(P);
-    const int n = static_cast<int>(S.v->ntab);
-    for (int j = 0; j < n; ++j)
-      if (S.tab_tok[j] == tl) return j;
+    if constexpr (kExtTable) {
+      const int n = *ext_n;
+      for (int j = 0; j < n; ++j)
+        if (ext_tok[j] == tl) return j;
+    } else {
+      const Smem S = smem_view(P);
+      const int n = static_cast<int>(S.v->ntab);
+      for (int j = 0; j < n; ++j)
+        if (S.tab_tok[j] == tl) return j;
+    }
     return -1;
   }
 
   // Exact value in the log-prob domain for local column tl whose raw logit is x.
   __device__ __forceinline__ float exact_y(const RowCtx& c, float x, int tl) const {
-    const Smem S = smem_view(P);
     if (P.mode == kModeProcessed) {
       if (c.excl && flagged(c, tl)) {
         const int j = table_find(tl);
-        if (j >= 0) return S.tab_y[j];
+        if (j >= 0) {
+          if constexpr (kExtTable) return ext_y[j];
+          else return smem_view(P).tab_y[j];
+        }
       }
       return (c.teff == 1.0f) ? x : __fdiv_rn(x, c.teff);
     }
@@ -507,19 +541,22 @@ struct Step {
     return Lm + __logf(tot);
   }
 
-  // Lowest y a streamed element needs to reach the request bound tau: its score
-  // cum + (y - lse) must reach tau's score, and lse >= L.  -inf without a bound.
   __device__ __forceinline__ float tau_floor(const RowCtx& c, uint64_t tau, float L) const {
-    if (tau == 0ull || !(L > -kInf && L < kInf)) return -kInf;
-    const float ts = key_score(tau);
-    const float f = ts - c.cum + L;
-    if (!(f > -kInf && f < kInf)) return -kInf;
-    // margin for y vs the exact quotient, the approximate logarithms and the
-    // roundings of the score sum (relative to the magnitudes of its terms)
-    return f - 1.0e-5f * (fabsf(f) + fabsf(ts) + fabsf(c.cum) + fabsf(L)) - 1e-30f;
+    return tau_floor_value(tau, c.cum, L);
   }
 
   // ---- selection helpers ------------------------------------------------------
+  // The key list's length as every thread reads it between two barriers: the
+  // same value everywhere (the decisions taken on it are uniform), and no
+  // thread appends again before all of them have read it.
+  __device__ __forceinline__ int list_len_sync() const {
+    const Smem S = smem_view(P);
+    csync();
+    const int n = static_cast<int>(S.v->cnt);
+    csync();
+    return n;
+  }
+
   // Reduce the shared key list to its best k (k < cnt).  Returns the cut.
   __device__ Cut shrink_to(int k) {
     const Smem S = smem_view(P);
@@ -771,8 +808,8 @@ struct Step {
           warp_append_n<8>(mask, kv, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
         }
         if (threadIdx.x == 0 && tau_g > S.v->thr_key) S.v->thr_key = tau_g;
-        csync();
-        if (base + kBatch < d0 + deg && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
+        const int n_list = list_len_sync();
+        if (base + kBatch < d0 + deg && n_list > kKeyCap - kBatch) {
           const Cut cut = shrink_to(P.k2);
           raise_tau(c.r, cut.floor_key());
         }
@@ -800,8 +837,8 @@ struct Step {
           if (kv[0] >= thr) mask = 1u;
         }
         warp_append_n<1>(mask, kv, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
-        csync();
-        if (base + kThreads < nloc && static_cast<int>(S.v->cnt) > kKeyCap - kThreads) {
+        const int n_list = list_len_sync();
+        if (base + kThreads < nloc && n_list > kKeyCap - kThreads) {
           const Cut cut = shrink_to(P.k2);
           raise_tau(c.r, cut.floor_key());
         }
@@ -861,8 +898,8 @@ struct Step {
           warp_append_n<kPer>(mask, kv, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
         }
         if (threadIdx.x == 0 && tau_g > S.v->thr_key) S.v->thr_key = tau_g;
-        csync();
-        if (end < c1 && static_cast<int>(S.v->cnt) > kKeyCap - kBatch) {
+        const int n_list = list_len_sync();
+        if (end < c1 && n_list > kKeyCap - kBatch) {
           const Cut cut = shrink_to(P.k2);
           raise_tau(c.r, cut.floor_key());
         }
@@ -936,8 +973,8 @@ struct Step {
         }
       }
       warp_append_n<kMaxPer>(mask, kv, S.keys, &S.v->cnt, kKeyCap, &S.v->overflow);
-      csync();
-      if (base + nb < P.VL && static_cast<int>(S.v->cnt) > kKeyCap - nb) thr = shrink_to(k).floor_key();
+      const int n_list = list_len_sync();
+      if (base + nb < P.VL && n_list > kKeyCap - nb) thr = shrink_to(k).floor_key();
     }
     if (static_cast<int>(S.v->cnt) > k) shrink_to(k);
   }
@@ -1528,8 +1565,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
     uint32_t cnt_prev = 0;
     float row_L = -kInf;
     if (bounded) {
-      csync();
-      cnt_prev = S.v->cnt;
+      cnt_prev = static_cast<uint32_t>(st.list_len_sync());
     }
     // shrink the row's list back to its best kk keys; the kk-th bounds the rest of the row
     auto shrink_row = [&]() {
@@ -1724,8 +1760,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
           if (lane == 31) base = atomicAdd(&S.v->cnt, wtot);
           base = __shfl_sync(0xFFFFFFFFu, base, 31);
         }
-        csync();
-        const uint32_t cnt_now = S.v->cnt;
+        const uint32_t cnt_now = static_cast<uint32_t>(st.list_len_sync());
         GR_PROF_VAL(12, cnt_now - cnt_prev);
         GR_PROF_VAL(14, floor_y > -kInf ? 1 : 0);
         GR_PROF_CNT(15);
@@ -1767,10 +1802,9 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
               }
               st.template process<EPV>(c, x, tbase + v * EPV, valid, m, s, thr_y, thr_key, floor_y, false);
             }
-            csync();
-            if (static_cast<int>(S.v->cnt) > kKeyCap - P.sub_vecs * EPV) shrink_row();
+            if (st.list_len_sync() > kKeyCap - P.sub_vecs * EPV) shrink_row();
           }
-          cnt_prev = S.v->cnt;
+          cnt_prev = static_cast<uint32_t>(st.list_len_sync());
         }
         if (cnt_prev > shrink_at) {
           csync();
@@ -1808,8 +1842,7 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
             }
             st.template process<EPV>(c, x, tbase + v * EPV, valid, m, s, thr_y, thr_key);
           }
-          csync();
-          if (static_cast<int>(S.v->cnt) > kKeyCap - P.sub_vecs * EPV) shrink_row();
+          if (st.list_len_sync() > kKeyCap - P.sub_vecs * EPV) shrink_row();
         }
       }
       __syncwarp();
@@ -1945,6 +1978,7 @@ drain:
 }
 
 #include "gr_step_ws.cuh"
+#include "gr_step_select_ws.cuh"
 
 // ---------------------------------------------------------------- merge kernel
 // One CTA of kThreads threads per request: gathers the request's per-row
@@ -2285,6 +2319,7 @@ struct DeviceInfo {
   int major = 0;
   bool attr_set[3] = {false, false, false};
   bool ws_attr_set[3] = {false, false, false};
+  bool sel_attr_set[3] = {false, false, false};
   bool merge_attr_set = false;
 };
 
@@ -2325,6 +2360,16 @@ static int device_info(DeviceInfo** out) {
 static size_t ws_tau_bytes(int R) { return align128(size_t(R) * 8 + 8); }   // + the row counter
 static size_t ws_cnt_bytes(int R, int NB) { return align128(size_t(R) * NB * 4); }
 static size_t ws_meta_bytes(int R, int NB) { return align128(size_t(R) * NB * kMetaWords * 4); }
+// Penalty tables of the selecting kernel: steps with processed log-probs, a
+// history of at most sel::kPenCap tokens and no per-beam top-K.
+static int ws_tab_words(const gr_step_desc* d) {
+  const bool used = d->logprobs_mode == GR_LOGPROBS_PROCESSED && d->hist_len >= 1 &&
+                    d->hist_len <= sel::kPenCap && d->per_beam_k == 0;
+  return used ? (d->hist_len + 31) / 32 * 32 : 0;
+}
+static size_t ws_tab_bytes(const gr_step_desc* d) {
+  return align128(size_t(d->num_requests) * d->num_beams * 2 * size_t(ws_tab_words(d)) * 4);
+}
 
 static int validate(const gr_step_desc* d) {
   if (!d) return GR_ERR_NULL;
@@ -2491,10 +2536,19 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 }
 
 // The warp-specialised kernel takes steps whose rows need no streamed
-// selection and no penalty exclusion.  GR_BEAM_KERNEL=stream|ws forces one
-// kernel (ws only where eligible); anything else selects automatically.
+// selection and no penalty exclusion; the selecting one steps without a
+// catalog (every row streamed) within its table and list limits.
+// GR_BEAM_KERNEL=stream|ws|select forces one kernel (ws and select only where
+// eligible); anything else selects automatically.
 static bool ws_eligible(const Params& P) {
   return P.K == 0 && !(P.mode == kModeProcessed && P.pen && P.T > 0);
+}
+
+static bool select_eligible(const Params& P, int es) {
+  if (P.K != 0 || P.N != 0 || P.partial_only || P.lse_in != nullptr) return false;
+  if (P.pen && P.T > 0 && P.mode == kModeProcessed && P.T > sel::kPenCap) return false;
+  if (P.kk + kThreads * (es == 4 ? 4 : 8) > kKeyCap) return false;            // one selection round beside kk keys
+  return static_cast<long long>(P.VL) * es <= static_cast<long long>(sel::kMaxRowStages) * sel::kStage;
 }
 
 static int kernel_choice() {
@@ -2502,7 +2556,40 @@ static int kernel_choice() {
   if (e == nullptr) return 0;
   if (std::strcmp(e, "stream") == 0) return 1;
   if (std::strcmp(e, "ws") == 0) return 2;
+  if (std::strcmp(e, "select") == 0) return 3;
   return 0;
+}
+
+template <typename TL>
+static int launch_fused_select(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream_t stream) {
+  int stages = 0;
+  for (int st = kMaxStages; st >= 3; --st) {
+    if (sel::smem_bytes(st) <= static_cast<size_t>(dev->smem_optin)) {
+      stages = st;
+      break;
+    }
+  }
+  if (stages == 0) return launch_fused<TL>(P, dev, dtype_idx, stream);
+  P.stages = stages;
+  const size_t smem = sel::smem_bytes(stages);
+  std::unique_lock<std::mutex> attr_lock(g_dev_mu);
+  if (!dev->sel_attr_set[dtype_idx]) {
+    if (cudaFuncSetAttribute(fused_select_ws_kernel<TL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             dev->smem_optin) != cudaSuccess)
+      return GR_ERR_CUDA;
+    dev->sel_attr_set[dtype_idx] = true;
+  }
+  attr_lock.unlock();
+  const int total = P.R * P.NB;
+  // the rows' penalty tables first (one warp per row), when penalties apply
+  if (!sel::pen_used(P)) P.pen_tab = nullptr;
+  if (P.pen_tab != nullptr &&
+      launch_pdl(pen_table_kernel<TL>, dim3((total + 7) / 8), dim3(256), 0, stream, P) != cudaSuccess)
+    return GR_ERR_CUDA;
+  const int grid = total < dev->sms ? total : dev->sms;
+  if (launch_pdl(fused_select_ws_kernel<TL>, dim3(grid), dim3(sel::kBlockSel), smem, stream, P) != cudaSuccess)
+    return GR_ERR_CUDA;
+  return GR_OK;
 }
 
 template <typename TL>
@@ -2535,6 +2622,10 @@ static int launch_fused_ws(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream
 template <typename TL>
 static int launch_step_kernel(Params& P, DeviceInfo* dev, int dtype_idx, cudaStream_t stream) {
   const int choice = kernel_choice();
+  // steps without a catalog: the selecting kernel (its streamers never wait
+  // on the selection)
+  if ((choice == 0 || choice == 3) && select_eligible(P, sizeof(TL)))
+    return launch_fused_select<TL>(P, dev, dtype_idx, stream);
   // a given lse (vocab-sharded phase 2) leaves only row-end work: the streaming
   // kernel puts every consumer warp on it (GR_BEAM_KERNEL=ws keeps the other)
   const bool ws = ws_eligible(P) && (P.lse_in == nullptr ? choice != 1 : choice == 2);
@@ -2603,6 +2694,9 @@ static int setup_step(const gr_step_desc* d, const gr_step_io* io, void* workspa
   *lse_ws = reinterpret_cast<float*>(ws + o);
   o += align128(size_t(R) * NB * 4);
   P.req_hist = (P.k2 >= kReqHistMinK2) ? reinterpret_cast<unsigned int*>(ws + o) : nullptr;
+  o += align128(size_t(R) * kReqHistBins * 4);
+  P.tabw = ws_tab_words(d);
+  P.pen_tab = (P.tabw > 0) ? reinterpret_cast<int*>(ws + o) : nullptr;
   const int rows = R * NB;
   row_meta_kernel<<<(rows + 255) / 256, 256, 0, s>>>(P);
   if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
@@ -2658,7 +2752,7 @@ int32_t gr_beam_step_workspace_size(const gr_step_desc* d, size_t* bytes) {
   *bytes = ws_tau_bytes(d->num_requests) + ws_cnt_bytes(d->num_requests, d->num_beams) +
            ws_meta_bytes(d->num_requests, d->num_beams) + align128(slots * 8) +
            align128(size_t(d->num_requests) * d->num_beams * 4) +
-           align128(size_t(d->num_requests) * kReqHistBins * 4);
+           align128(size_t(d->num_requests) * kReqHistBins * 4) + ws_tab_bytes(d);
   return GR_OK;
 }
 

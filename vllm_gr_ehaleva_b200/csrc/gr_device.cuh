@@ -137,6 +137,13 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
   return pol;
 }
+// A relaxed GPU-scope 64-bit load: sees other CTAs' atomics, and orders
+// nothing around it (a volatile access would keep later loads behind it).
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
 __device__ __forceinline__ void st_keep_u64(unsigned long long* p, unsigned long long v, uint64_t pol) {
   asm volatile("st.global.L2::cache_hint.u64 [%0], %1, %2;" ::"l"(p), "l"(v), "l"(pol) : "memory");
 }

@@ -539,8 +539,7 @@ __device__ void ws_finish_rows(const Params& P) {
           }
           st.template process<EPV>(c, x, g.head + v * EPV, valid, dm, ds, thr_y, thr_key, tau_off);
         }
-        csync();
-        if (static_cast<int>(S.v->cnt) > kKeyCap - P.sub_vecs * EPV) {
+        if (st.list_len_sync() > kKeyCap - P.sub_vecs * EPV) {
           const Cut cut = st.shrink_to(P.kk);
           if (tid == 0) {
             S.v->discard = 1;
