@@ -101,3 +101,16 @@ def test_streamed_rows_behind_the_request_bound(dtype, mode):
         nxt = next_inputs(case, gpu, make_logits(R, B, V, 3.0, 411 + step, dtype))
         nxt.hist = case.hist      # a fixed penalty history (none in raw mode)
         case = nxt
+
+
+def test_streamed_rows_whose_scores_rise_behind_the_bound():
+    # beams are taken in order, and here every later beam scores far above the
+    # bound its predecessors set: the survivors of a row that started with the
+    # bound overflow its slot (they go on in the selectors' list) or that list
+    # too (the row is read again exactly)
+    R, B, V = 2, 256, 8192
+    cum = np.tile(np.arange(B, dtype=np.float32), (R, 1)).astype(np.float32)
+    case = Case(logits32=make_logits(R, B, V, 3.0, 420, "f32"), dtype="f32", cum=cum,
+                node=np.full((R, B), -1, np.int32), beam_width=B, vocab_size=V)
+    gpu = gpu_step(case)
+    assert_step_parity(case, gpu, label="rising scores")

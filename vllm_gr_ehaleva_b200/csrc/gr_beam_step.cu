@@ -1789,6 +1789,8 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
           if (tid == 0) S.v->cnt = cnt_prev;
           csync();
           for (int sb = 0; sb < nvec; sb += P.sub_vecs) {
+            // room for a whole sub-batch first (the list may hold up to shrink_at keys)
+            if (st.list_len_sync() > kKeyCap - P.sub_vecs * EPV) shrink_row();
             const int send = min(nvec, sb + P.sub_vecs);
             for (int vb = sb + warp * 32; vb < send; vb += kThreads) {
               const int v = vb + lane;
@@ -1802,7 +1804,6 @@ __global__ void __launch_bounds__(kBlock, 2) fused_step_kernel(const __grid_cons
               }
               st.template process<EPV>(c, x, tbase + v * EPV, valid, m, s, thr_y, thr_key, floor_y, false);
             }
-            if (st.list_len_sync() > kKeyCap - P.sub_vecs * EPV) shrink_row();
           }
           cnt_prev = static_cast<uint32_t>(st.list_len_sync());
         }

@@ -67,6 +67,7 @@ constexpr uint32_t kHashEmpty = 0xFFFFFFFFu;
 enum : int { kEndSelectors = 0, kEndFinisher = 1 };
 static_assert(kStageVecs % kThreads == 0 && kStageVecs == kStrThreads * kVecPerThread, "stage split");
 static_assert(kSelVecs * 8 <= 64, "one 64-bit survivor mask per selector thread and stage");
+static_assert(kVecPerThread * 8 <= 32, "one 32-bit element mask per streaming thread and stage");
 
 // Per-slot block: record, published and final streamer partials, penalty table and flags.
 struct Slot {
@@ -79,15 +80,16 @@ struct Slot {
                                 // the row's lse (raised with atomicMax, so it never goes down)
   int stages_done;              // stages whose combined bound lse_ord covers
   uint32_t kcnt;                // rows started with the request's bound: survivors reserved in `keys`
-  int kovf;                     // such a row's reservation did not fit `keys`
+  int kovf;                     // such a row's survivors did not all fit `keys` (the selectors end it)
+  int kfail;                    // the first reservation that did not fit: keys [0, kfail) are written
   int end_by;                   // kEndSelectors / kEndFinisher
-  int pad[26];
+  int pad[25];
   int sprog[kMaxRowStages];     // streaming warps that have published each stage
   int tab_tok[kPenCap];         // penalised local columns
   float tab_y[kPenCap];         // their processed values
   uint32_t flags[kFlagWords];   // bit stage * kStrThreads + t: streaming thread t's vectors of that stage hold one
   uint32_t hkey[kHash];         // such a (stage * kStrThreads + t), or kHashEmpty
-  uint32_t hmask[kHash];        // its bit j * EPV + e: element e of the thread's vector j is penalised
+  uint32_t hmask[kHash];   // its bit j * EPV + e: element e of the thread's vector j is penalised
   unsigned long long keys[kSlotKeys];   // value keys ord(y) | ~flat of those rows
 };
 
@@ -344,6 +346,7 @@ __device__ void sel_produce(const Params& P) {
       sl->stages_done = 0;
       sl->kcnt = 0u;
       sl->kovf = 0;
+      sl->kfail = sel::kSlotKeys;
       sl->end_by = sel::kEndSelectors;
     }
     __syncwarp();   // the flags are zero before any lane sets one
@@ -688,7 +691,6 @@ __device__ void sel_select_rows(const Params& P) {
     uint64_t* const kbuf = in_slot ? reinterpret_cast<uint64_t*>(sl->keys) : S.keys;
     uint32_t* const kcnt = in_slot ? &sl->kcnt : &S.v->cnt;
     const uint32_t kcap = in_slot ? static_cast<uint32_t>(sel::kSlotKeys) : static_cast<uint32_t>(kKeyCap);
-    int* const kovf = in_slot ? &sl->kovf : &S.v->overflow;
     float thr_y = -kInf;
     const Geom g = row_geom<ES, sel::kStage>(P, c.row);
     const uint32_t vb = static_cast<uint32_t>(c.b) * static_cast<uint32_t>(P.V);
@@ -708,7 +710,7 @@ __device__ void sel_select_rows(const Params& P) {
             pred = true;
           }
         }
-        warp_append(pred, key, kbuf, kcnt, kcap, kovf);
+        warp_append(pred, key, kbuf, kcnt, kcap, &S.v->overflow);
       }
       csync();
     }
@@ -824,7 +826,21 @@ __device__ void sel_select_rows(const Params& P) {
             if (lane == 31) base = atomicAdd(kcnt, wtot);
             SEL_CNT(lane == 31, 14, wtot);
             base = __shfl_sync(0xFFFFFFFFu, base, 31);
-            if (base + wtot <= kcap) {
+            uint64_t* dst = kbuf;
+            bool fits = base + wtot <= kcap;
+            if (!fits && in_slot) {
+              // the slot is full (a weak bound): the row's further survivors go
+              // to the selectors' list, and the selectors end the row
+              if (lane == 31) {
+                atomicMin(&sl->kfail, static_cast<int>(base));
+                sl->kovf = 1;
+                base = atomicAdd(&S.v->cnt, wtot);
+              }
+              base = __shfl_sync(0xFFFFFFFFu, base, 31);
+              dst = S.keys;
+              fits = base + wtot <= static_cast<uint32_t>(kKeyCap);
+            }
+            if (fits) {
               uint32_t pos = base + inc - cl;
               uint64_t mk = pm;
               while (mk) {
@@ -833,10 +849,10 @@ __device__ void sel_select_rows(const Params& P) {
                 const int col = (tid + (bi / EPV) * kThreads) * EPV + (bi % EPV);
                 const float x = Tr::load_s(stage_p, col);
                 const float ye = (P.mode == kModeProcessed && c.teff != 1.0f) ? __fdiv_rn(x, c.teff) : x;
-                kbuf[pos++] = make_key(ye, vb + static_cast<uint32_t>(tok_of(P, tbase + col)));
+                dst[pos++] = make_key(ye, vb + static_cast<uint32_t>(tok_of(P, tbase + col)));
               }
             } else if (lane == 0) {
-              *reinterpret_cast<volatile int*>(kovf) = 1;
+              *reinterpret_cast<volatile int*>(&S.v->overflow) = 1;   // the row is read again exactly
             }
           }
           SEL_ADD(tid == 0, 2, t_scan);
@@ -932,17 +948,11 @@ __device__ void sel_select_rows(const Params& P) {
     // others end here: the normaliser from the streamers' partials and the
     // table, then the candidates
     SEL_T(t_end);
-    // the streamers' partials and, for rows with the bound, their survivors
-    ok = mbar_wait_bounded(&W.rowdone[q], par, &S.v->abort);
-    if (!ok) {
-      if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
-      S.v->abort = 1;
-    }
     if (tid == 0) W.sel_abort[q] = S.v->abort;
     csync();
     if (W.sel_abort[q]) break;
     const int row_keys = static_cast<int>(sl->kcnt) + ((cand && c.excl) ? pen_n : 0);
-    if ((in_slot || !cand) && !sl->kovf && row_keys <= min(P.k2, sel::kSlotKeys)) {
+    if ((in_slot || !cand) && !sl->kovf && !S.v->overflow && row_keys <= min(P.k2, sel::kSlotKeys)) {
       if (tid == 0) {
         sl->end_by = sel::kEndFinisher;
         mbar_arrive(&W.handoff[q]);   // release: the slot's keys
@@ -951,14 +961,24 @@ __device__ void sel_select_rows(const Params& P) {
     }
     SEL_CNT(tid == 0, 13, 1);
     if (in_slot) {
-      // the slot's keys join the selectors' list (an overflowed slot: the row is read again)
-      const int n = min(static_cast<int>(sl->kcnt), sel::kSlotKeys);
-      for (int i = tid; i < n; i += kThreads) S.keys[i] = sl->keys[i];
-      if (tid == 0) {
-        S.v->cnt = static_cast<uint32_t>(n);
-        S.v->overflow = sl->kovf;
+      // the slot's written keys join the selectors' list (beside the survivors
+      // that did not fit the slot; a full list: the row is read again)
+      const int n = min(static_cast<int>(sl->kcnt), sl->kfail);
+      const int b0 = static_cast<int>(S.v->cnt);
+      if (b0 + n <= kKeyCap) {
+        for (int i = tid; i < n; i += kThreads) S.keys[b0 + i] = sl->keys[i];
       }
       csync();
+      if (tid == 0) {
+        if (b0 + n <= kKeyCap) S.v->cnt = static_cast<uint32_t>(b0 + n);
+        else S.v->overflow = 1;
+      }
+      csync();
+    }
+    ok = mbar_wait_bounded(&W.rowdone[q], par, &S.v->abort);   // the streamers' partials
+    if (!ok) {
+      if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
+      S.v->abort = 1;
     }
     static_assert(sel::kStrWarps <= 32, "one partial per lane");
     float pm_ = (lane < sel::kStrWarps) ? sl->part_m[lane] : -kInf;
