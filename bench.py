@@ -228,6 +228,12 @@ def initial_state(wl, device):
     return cum, node, hist
 
 
+def pen_tables_launched(wl) -> bool:
+    """The selecting kernel runs pen_table_kernel first for processed-mode
+    steps with penalties (step_kwargs passes them in that mode)."""
+    return step_kernel_name(wl) == "fused_select_ws_kernel" and wl["cfg"]["mode"] == "processed"
+
+
 def step_kernel_name(wl) -> str:
     """The step kernel the library picks for this workload: the selecting
     warp-specialised kernel for steps without a catalog, else the
@@ -388,12 +394,14 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": None,
-                     "kernel": f"gr::{step_kernel_name(wl)} (timed as the whole step: row_meta + fused + merge)",
+                     "kernel": f"gr::{step_kernel_name(wl)} (timed as the whole step: row_meta + [pen_table] + step kernel + merge)",
                      "algorithmic_bytes_per_launch": int(np.mean(steps_bytes)),
                      "avg_launch_ms": round(avg_launch_ms, 5), "per_level_ms": per_level_ms,
                      "per_level_ms_min_max": per_level_range,
                      "per_level_bytes": [int(b) for b in bytes_cycle]},
-        "gpu_launches": 3 * args.steps,          # row_meta_kernel + fused_step_kernel + merge_kernel per step
+        # row_meta_kernel + the step kernel + merge_kernel per step, and
+        # pen_table_kernel before the selecting kernel when penalties apply
+        "gpu_launches": (4 if pen_tables_launched(wl) else 3) * args.steps,
         "clocks": clk,
         "device_errors": err,
     }
