@@ -26,7 +26,13 @@ constexpr int kBatch = 2048;                  // max insertions between capacity
 constexpr int kPenTableMax = 1024;            // max history tokens with penalties
 constexpr int kSlack = 64;                    // extra keys kept by streamed top-k
 constexpr int kMaxBitmapWords = 8192;         // penalties: local vocab <= 262144
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s per wait
+// Longest time any wait of the step kernels spins before it gives up with
+// GR_DEVERR_TIMEOUT (a build may set it lower, e.g. -DGR_WAIT_LIMIT_NS=1000000
+// for 1 ms in a test build).
+#ifndef GR_WAIT_LIMIT_NS
+#define GR_WAIT_LIMIT_NS 2000000000ull
+#endif
+constexpr unsigned long long kWaitLimitNs = GR_WAIT_LIMIT_NS;   // 2 s per wait by default
 constexpr uint32_t kWaitSleepNs = 100000u;                    // longest sleep per try (0.1 ms)
 
 constexpr float kLog2e = 1.4426950408889634f;
