@@ -115,8 +115,15 @@ typedef struct gr_step_desc {
                              j * vocab_stride (0 or 1: a contiguous slice;
                              S with vocab_offset = k: shard k of a strided
                              split over S ranks, tokens k, k + S, ...)      */
-  int32_t reserved;       /* 0                                                */
+  int32_t flags;          /* GR_STEP_* bits (0: none)                         */
 } gr_step_desc;
+
+/* gr_step_desc.flags (gr_beam_step / gr_beam_step_noalloc; the vocab-sharded
+ * entry points take 0).  GR_STEP_CLEAR_ERR: the step sets *io->err to 0
+ * before any of its kernels reports into it, so the caller need not zero the
+ * word first (one launch less per step); without it device errors are OR-ed
+ * into the word as it stands. */
+#define GR_STEP_CLEAR_ERR 0x1
 
 typedef struct gr_step_io {
   /* inputs */

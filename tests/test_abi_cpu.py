@@ -83,6 +83,25 @@ def test_workspace_size_validation(kw, status):
         assert n.value >= 2 * 8 + 2 * 4 * 4 + 2 * 4 * 8 * 8
 
 
+def test_step_flags_validated_without_a_device():
+    lib = _lib.load()
+    n = ctypes.c_size_t(0)
+    d = _desc()
+    d.flags = _lib.GR_STEP_CLEAR_ERR
+    assert lib.gr_beam_step_workspace_size(ctypes.byref(d), ctypes.byref(n)) == 0
+    d.flags = 0x2                                   # no such flag
+    assert lib.gr_beam_step_workspace_size(ctypes.byref(d), ctypes.byref(n)) == -2
+    # the vocab-sharded calls share one error word across three calls: no flags there
+    d.flags = _lib.GR_STEP_CLEAR_ERR
+    io = _lib.StepIO()
+    part = ctypes.c_float(0.0)
+    assert lib.gr_lse_partials(ctypes.byref(d), ctypes.byref(io), ctypes.byref(part), None, 0, None) == -2
+    keys = ctypes.c_uint64(0)
+    assert lib.gr_shard_candidates(ctypes.byref(d), ctypes.byref(io), ctypes.byref(part), 2, ctypes.byref(keys),
+                                   None, 0, None) == -2
+    assert lib.gr_merge_candidates(ctypes.byref(d), ctypes.byref(io), ctypes.byref(keys), 2, None, 0, None) == -2
+
+
 def test_null_arguments_rejected_before_any_device_work():
     lib = _lib.load()
     d = _desc()

@@ -11,6 +11,7 @@ import os
 from .build import LIB_PATH
 
 GR_OK = 0
+GR_STEP_CLEAR_ERR = 0x1      # gr_step_desc.flags: the step zeroes io->err itself
 STATUS_NAMES = {
     0: "GR_OK", -1: "GR_ERR_NULL", -2: "GR_ERR_BAD_DESC", -3: "GR_ERR_DTYPE",
     -4: "GR_ERR_MISALIGNED", -5: "GR_ERR_WORKSPACE", -6: "GR_ERR_UNSUPPORTED",
@@ -50,7 +51,7 @@ class StepDesc(ctypes.Structure):
         ("num_nodes", ctypes.c_int32),
         ("num_edges", ctypes.c_int64),
         ("vocab_stride", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
     ]
 
 

@@ -120,6 +120,7 @@ struct Params {
   int win_bytes; // child window bytes (0: no constrained rows in the step)
   int partial_only;   // 1: write (max, sumexp) partials only (vocab-sharded phase 1)
   int stall_copies;   // test hook: the producer issues no copies, so the bounded waits run out
+  int clear_err;      // GR_STEP_CLEAR_ERR: row_meta_kernel zeroes *err; bad nodes are reported by the merge
   float2* partials;
   const float* lse_in;            // vocab-sharded phase 2: the rows' global normaliser (no streaming)
   unsigned long long* keys_out;   // merge writes the sorted top-2B keys [R][2B] (zero padded) instead
@@ -175,7 +176,8 @@ enum MetaWord {
   kMRow = 8, kMR = 9, kMB = 10,                                     // row, request, beam
   kMRef = 11,                                                       // the request's first beam's cum
   kMToks = 12,                                                      // child tokens of small nodes (16 words)
-  kMTauLo = 28, kMTauHi = 29                                        // request threshold (filled on chip)
+  kMTauLo = 28, kMTauHi = 29,                                       // request threshold (filled on chip)
+  kMBad = 30                                                        // the row's node id was out of range
 };
 static_assert(kMToks + kMetaSmall <= kMTauLo, "record layout");
 
@@ -1388,13 +1390,18 @@ __global__ void __launch_bounds__(256) row_meta_kernel(const __grid_constant__ P
     P.tau[row / P.NB] = 0ull;     // the request's running bound starts empty
     P.rowcnt[row] = 0u;           // and its candidate list
   }
+  // GR_STEP_CLEAR_ERR: the error word starts at 0.  Nothing else in this grid
+  // writes it then (a bad node goes into its record, reported by the merge),
+  // and every later kernel writes it only after waiting for this grid.
+  if (P.clear_err && row == 0) *P.err = 0;
   if (row == 0) *P.row_counter = 0u;
   int w[kMetaWords];
 #pragma unroll
   for (int i = 0; i < kMetaWords; ++i) w[i] = 0;
   int node = P.node[row];
   if (node < GR_NODE_DEAD || node >= P.N) {
-    atomicOr(P.err, GR_DEVERR_BAD_NODE);
+    if (P.clear_err) w[kMBad] = 1;
+    else atomicOr(P.err, GR_DEVERR_BAD_NODE);
     node = GR_NODE_DEAD;
   }
   const int r = row / P.NB;
@@ -2054,6 +2061,12 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
   const int NB = P.NB, k2 = P.k2;
   const int S = P.slot_rows;   // slots gathered per request (rows, or shards)
   pdl_wait();   // the step kernel's row slots, counts and bounds
+  if (P.clear_err) {
+    // GR_STEP_CLEAR_ERR: the bad node ids row_meta_kernel found in this
+    // request's rows (its records are complete: the step kernel waited for it)
+    for (int b = tid; b < NB; b += blockDim.x)
+      if (P.meta[(static_cast<size_t>(r) * NB + b) * kMetaWords + kMBad]) atomicOr(P.err, GR_DEVERR_BAD_NODE);
+  }
 #ifdef GR_PHASE_PROFILE
   long long mt[8];
   int mq = 0;
@@ -2376,6 +2389,7 @@ static int validate(const gr_step_desc* d) {
   if (!d) return GR_ERR_NULL;
   if (d->num_requests < 1 || d->num_beams < 1 || d->beam_width < 1) return GR_ERR_BAD_DESC;
   if (d->vocab_size < 1 || d->vocab_local < 1 || d->vocab_offset < 0 || d->vocab_stride < 0) return GR_ERR_BAD_DESC;
+  if (d->flags & ~GR_STEP_CLEAR_ERR) return GR_ERR_BAD_DESC;
   // the last local column's token: vocab_offset + (vocab_local - 1) * stride < vocab_size
   const long long vstride = d->vocab_stride > 1 ? d->vocab_stride : 1;
   if (static_cast<long long>(d->vocab_offset) + (d->vocab_local - 1) * vstride >= d->vocab_size) return GR_ERR_BAD_DESC;
@@ -2459,6 +2473,7 @@ static void fill_params(Params& P, const gr_step_desc* d, const gr_step_io* io) 
   P.win_bytes = (d->num_nodes > 0 && P.K == 0) ? kWinBytes : 0;
   P.partial_only = 0;
   P.stall_copies = stall_copies_requested();
+  P.clear_err = (d->flags & GR_STEP_CLEAR_ERR) ? 1 : 0;
   P.partials = nullptr;
   P.lse_in = nullptr;
   P.keys_out = nullptr;
@@ -2828,6 +2843,7 @@ int32_t gr_lse_partials(const gr_step_desc* d, const gr_step_io* io, float* part
                         size_t workspace_bytes, void* stream) {
   gr::NvtxRange nvtx_range("gr_lse_partials");
   if (!partials) return GR_ERR_NULL;
+  if (d && d->flags != 0) return GR_ERR_BAD_DESC;   // flags are for the single-call step
   Params P;
   DeviceInfo* dev = nullptr;
   float* lse_ws = nullptr;
@@ -2847,6 +2863,7 @@ int32_t gr_shard_candidates(const gr_step_desc* d, const gr_step_io* io, const f
   gr::NvtxRange nvtx_range("gr_shard_candidates");
   if (!gathered_partials || !shard_keys) return GR_ERR_NULL;
   if (num_shards < 1) return GR_ERR_BAD_DESC;
+  if (d && d->flags != 0) return GR_ERR_BAD_DESC;
   if (d && d->per_beam_k != 0) return GR_ERR_UNSUPPORTED;
   Params P;
   DeviceInfo* dev = nullptr;
@@ -2871,6 +2888,7 @@ int32_t gr_merge_candidates(const gr_step_desc* d, const gr_step_io* io, const u
   gr::NvtxRange nvtx_range("gr_merge_candidates");
   if (!gathered_keys) return GR_ERR_NULL;
   if (num_shards < 1 || num_shards > 65535) return GR_ERR_BAD_DESC;
+  if (d && d->flags != 0) return GR_ERR_BAD_DESC;
   if (d && d->per_beam_k != 0) return GR_ERR_UNSUPPORTED;
   Params P;
   DeviceInfo* dev = nullptr;

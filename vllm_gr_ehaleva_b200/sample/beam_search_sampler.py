@@ -105,9 +105,11 @@ def _prepare(logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor, *, bea
              logprobs_mode: str = "raw_logprobs", per_beam_k: int = 0, eos_token_id: Optional[int] = None,
              hist: Optional[torch.Tensor] = None, temperature=None, repetition_penalty=None,
              presence_penalty=None, frequency_penalty=None, workspace: Optional[Workspace] = None,
-             stream: Optional[torch.cuda.Stream] = None, vocab_stride: int = 1):
+             stream: Optional[torch.cuda.Stream] = None, vocab_stride: int = 1, clear_err: bool = False):
     """Checks the step inputs and builds (descriptor, io, outputs, workspace, stream).
-    Local logit column j holds token vocab_offset + j * vocab_stride."""
+    Local logit column j holds token vocab_offset + j * vocab_stride.  clear_err
+    (single-call steps): the library zeroes the error word itself
+    (GR_STEP_CLEAR_ERR), so it is allocated without a fill."""
     if not logits.is_cuda:
         raise ValueError("logits must be a CUDA tensor")
     device = logits.device
@@ -153,6 +155,8 @@ def _prepare(logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor, *, bea
     desc = make_desc(R=R, NB=NB, B=B, V=V, VL=VL, voff=int(vocab_offset), row_stride=int(row_stride),
                      dtype=_DTYPES[logits.dtype], mode=mode, K=int(per_beam_k), eos=eos, T=T, N=N, E=E,
                      VS=int(vocab_stride))
+    if clear_err:
+        desc.flags = _lib.GR_STEP_CLEAR_ERR
     temps = _per_request(temperature, R, device)
     reps = _per_request(repetition_penalty, R, device)
     press = _per_request(presence_penalty, R, device)
@@ -166,7 +170,7 @@ def _prepare(logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor, *, bea
         sel_token=torch.empty((R, B), **i32), sel_parent=torch.empty((R, B), **i32),
         sel_node=torch.empty((R, B), **i32), eos_score=torch.empty((R, NB), **f32),
         hist_out=torch.empty((R, B, T + 1), **i32), lse=torch.empty((R, NB), **f32),
-        err=torch.zeros(1, **i32))
+        err=torch.empty(1, **i32) if clear_err else torch.zeros(1, **i32))
     io = _lib.StepIO()
     io.logits, io.cum, io.node = _ptr(logits), _ptr(cum), _ptr(node)
     io.row_ptr, io.child_tok, io.child_node = _ptr(row_ptr), _ptr(child_tok), _ptr(child_node)
@@ -214,7 +218,7 @@ def beam_step(logits: torch.Tensor, cum: torch.Tensor, node: torch.Tensor, *, be
         logits, cum, node, beam_width=beam_width, csr=csr, vocab_size=vocab_size, vocab_offset=vocab_offset,
         logprobs_mode=logprobs_mode, per_beam_k=per_beam_k, eos_token_id=eos_token_id, hist=hist,
         temperature=temperature, repetition_penalty=repetition_penalty, presence_penalty=presence_penalty,
-        frequency_penalty=frequency_penalty, workspace=workspace, stream=stream)
+        frequency_penalty=frequency_penalty, workspace=workspace, stream=stream, clear_err=True)
     st = lib.gr_beam_step(ctypes.byref(desc), ctypes.byref(io), ctypes.c_void_p(ws.data_ptr()),
                           ctypes.c_size_t(ws.numel()), ctypes.c_void_p(s.cuda_stream))
     _lib.check(st, "gr_beam_step")
