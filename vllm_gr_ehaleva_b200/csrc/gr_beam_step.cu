@@ -687,7 +687,9 @@ struct Step {
         // (the (2B+1)-th when one child is EOS).  Scores are monotone in the
         // value, so every child scoring at least that value's score is kept,
         // and at least 2B children other than EOS do.
-        const Cut vc = cta_radix_select([this, d0](int j) { return win_value_key(d0 + j, j); }, deg, ksel, S.sel);
+        // (only the value bits are resolved: the bound needs the value alone)
+        const Cut vc = cta_radix_select([this, d0](int j) { return win_value_key(d0 + j, j); }, deg, ksel, S.sel,
+                                        ES == 4 ? 32 : 48);
         if (threadIdx.x == 0) {
           const float xt = value_of_key(vc.floor_key());
           const float st = __fadd_rn(__fadd_rn(c.cum, __fsub_rn(xt, lse)), 0.0f);

@@ -356,7 +356,7 @@ struct SelectScratch {
 // The k largest of n distinct keys (1 <= k <= n), MSB-first over 8-bit digits.
 // keyf(i) returns key i.  All threads of the CTA call this.
 template <class KeyFn>
-__device__ Cut cta_radix_select(KeyFn keyf, int n, int k, SelectScratch* sc) {
+__device__ Cut cta_radix_select(KeyFn keyf, int n, int k, SelectScratch* sc, int stop_shift = 0) {
   uint64_t prefix = 0;
   int shift = 64;
   int krem = k;
@@ -406,7 +406,8 @@ __device__ Cut cta_radix_select(KeyFn keyf, int n, int k, SelectScratch* sc) {
     csync();
     prefix |= static_cast<uint64_t>(d) << shift;
     krem -= static_cast<int>(above);
-    if (cnt == static_cast<uint32_t>(krem) || shift == 0) break;
+    // (stop_shift > 0: only the key's bits above stop_shift are resolved)
+    if (cnt == static_cast<uint32_t>(krem) || shift <= stop_shift) break;
   }
   return Cut{prefix, shift};
 }
