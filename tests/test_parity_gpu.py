@@ -160,6 +160,21 @@ def test_vocab_local_offset():
     assert_step_parity(case, gpu_step(case))
 
 
+def test_unconstrained_processed_column_slice():
+    # unconstrained processed rows on a column slice of the vocabulary: the
+    # penalty table keeps only the history tokens the slice holds
+    R, NB, B, V, H = 2, 8, 8, 12000, 32
+    off, VL = 5000, 4000
+    full = make_logits(R, NB, V, 3.0, 14, "f32")
+    hist = histories(R, NB, H, V, seed=6)
+    hist[:, :, :8] = off + 7 + np.arange(8, dtype=np.int32)   # some history inside the slice for sure
+    case = Case(logits32=np.ascontiguousarray(full[:, :, off:off + VL]), dtype="f32", cum=initial_cum(R, NB),
+                node=np.full((R, NB), -1, np.int32), beam_width=B, vocab_size=V, vocab_offset=off,
+                hist=hist, mode="processed_logprobs", temperature=[0.7, 1.3], rep=[1.2, 1.5], pres=[0.5, 0.1],
+                freq=[0.1, 0.0])
+    assert_step_parity(case, gpu_step(case))
+
+
 @pytest.mark.slow
 def test_full_vocab_cfg2_rows():
     # BASELINE cfg2 geometry (V=152064, B=128, bf16, 3-level codebook 8192) on 2 requests
