@@ -212,14 +212,17 @@ __global__ void __launch_bounds__(256) pen_table_kernel(const __grid_constant__ 
         cnt[k] = 0;
         first[k] = 1;
       }
+      const int groups = (P.T + 31) / 32;   // register groups that hold history tokens
 #pragma unroll
       for (int kk = 0; kk < kPer; ++kk) {
         for (int j = 0; j < 32 && kk * 32 + j < P.T; ++j) {   // position kk * 32 + j, uniform bounds
           const int o = __shfl_sync(0xFFFFFFFFu, tk[kk], j);
 #pragma unroll
           for (int k = 0; k < kPer; ++k) {
-            cnt[k] += (o == tk[k]);
-            if (kk * 32 + j < k * 32 + lane && o == tk[k]) first[k] = 0;
+            if (k < groups) {
+              cnt[k] += (o == tk[k]);
+              if (kk * 32 + j < k * 32 + lane && o == tk[k]) first[k] = 0;
+            }
           }
         }
       }
