@@ -654,12 +654,15 @@ __device__ void sel_select_rows(const Params& P) {
     sel::Slot* sl = W.slot(q);
     bool ok = mbar_wait_bounded(&W.recfull[q], par, &S.v->abort);
     if (!ok) {
-      // no record: leave (the streamers drain the copies in flight)
       if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
       S.v->abort = 1;
-      break;
     }
-    if (sl->rec[kMRow] < 0) break;
+    // one decision for every selector: no record (the streamers drain the
+    // copies in flight) or the stop record ends the loop for all
+    csync();
+    if (tid == 0) W.sel_abort[q] = (S.v->abort || sl->rec[kMRow] < 0) ? 1 : 0;
+    csync();
+    if (W.sel_abort[q]) break;
     RowCtx c;
     const int* rec = sl->rec;
     c.row = rec[kMRow];
@@ -983,6 +986,12 @@ __device__ void sel_select_rows(const Params& P) {
       if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
       S.v->abort = 1;
     }
+    // one decision before the partials are read: a thread whose wait gave up
+    // could otherwise take the exact normaliser's collective path alone
+    csync();
+    if (tid == 0) W.sel_abort[q] = S.v->abort ? 1 : 0;
+    csync();
+    if (W.sel_abort[q]) break;
     static_assert(sel::kStrWarps <= 32, "one partial per lane");
     float pm_ = (lane < sel::kStrWarps) ? sl->part_m[lane] : -kInf;
     float ps_ = (lane < sel::kStrWarps) ? sl->part_s[lane] : 0.0f;

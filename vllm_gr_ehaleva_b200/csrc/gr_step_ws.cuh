@@ -417,14 +417,24 @@ __device__ void ws_finish_rows(const Params& P) {
     const uint32_t par = static_cast<uint32_t>(it / ws::kSlots) & 1u;
     WS_PROF_T(t_rd);
     bool ok = mbar_wait_bounded(&W.recfull[slot], par, &S.v->abort);
-    // the stop record ends the loop for every finisher (all read the same word)
-    if (ok && W.rec(slot)[kMRow] < 0) break;
-    ok = ok && mbar_wait_bounded(&W.rowdone[slot], par, &S.v->abort);
-    ok = ok && mbar_wait_bounded(&W.winfull[slot], par, &S.v->abort);
+    // a stop record has no row behind it (no partials, no window)
+    if (!(ok && W.rec(slot)[kMRow] < 0)) {
+      ok = ok && mbar_wait_bounded(&W.rowdone[slot], par, &S.v->abort);
+      ok = ok && mbar_wait_bounded(&W.winfull[slot], par, &S.v->abort);
+    }
     if (!ok) {
       if (!S.v->abort) atomicOr(P.err, GR_DEVERR_TIMEOUT);
       S.v->abort = 1;
     }
+    // One decision for every finisher before any reads the row: a wait that
+    // gave up on one thread (its abort is visible after the barrier) or the
+    // stop record ends the loop for all.  Taken per thread, threads that left
+    // would be missing at the next barrier, and threads that read partials
+    // not yet written could disagree on the exact normaliser's collective path.
+    csync();
+    if (tid == 0) W.fin_abort[slot] = (S.v->abort || W.rec(slot)[kMRow] < 0) ? 1 : 0;
+    csync();
+    if (W.fin_abort[slot]) break;
     WS_PROF_ADD(tid == 0, 2, t_rd);
     WS_PROF_T(t_fin);
     RowCtx c;
