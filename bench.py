@@ -410,12 +410,13 @@ def run_ours(args):
     if cpu is not None:
         res["cpu_baseline"] = cpu
     # DRAM traffic per launch from the committed ncu summary (same kernel, same workload)
-    prof = os.path.join(ROOT, "profiles", f"fused_step_{args.config}.md")
-    if os.path.exists(prof) and R == CONFIGS[args.config]["requests"]:
-        with open(prof) as f:
-            for line in f:
-                if line.startswith(f"traffic_bytes_per_launch_{args.config}:"):
-                    res["roofline"]["traffic"] = int(line.split(":")[1])
+    for name in (f"fused_step_{args.config}.md", f"fused_select_{args.config}.md"):
+        prof = os.path.join(ROOT, "profiles", name)
+        if os.path.exists(prof) and R == CONFIGS[args.config]["requests"]:
+            with open(prof) as f:
+                for line in f:
+                    if line.startswith(f"traffic_bytes_per_launch_{args.config}:"):
+                        res["roofline"]["traffic"] = int(line.split(":")[1])
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:
