@@ -1386,6 +1386,9 @@ done:
 // nodes, every child token).
 __global__ void __launch_bounds__(256) row_meta_kernel(const __grid_constant__ Params P) {
   pdl_trigger();   // the step kernel may start its prologue; it waits for this grid before reading
+  // launched early as well (behind the previous step's merge, which reads this
+  // workspace): nothing is read or written before that grid is complete
+  pdl_wait();
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= P.R * P.NB) return;
   if (row % P.NB == 0) {
@@ -2063,6 +2066,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const __grid_constant__
   const int NB = P.NB, k2 = P.k2;
   const int S = P.slot_rows;   // slots gathered per request (rows, or shards)
   pdl_wait();   // the step kernel's row slots, counts and bounds
+  pdl_trigger();   // the next step's row records may launch (they wait for this grid)
   if (P.clear_err) {
     // GR_STEP_CLEAR_ERR: the bad node ids row_meta_kernel found in this
     // request's rows (its records are complete: the step kernel waited for it)
@@ -2716,8 +2720,7 @@ static int setup_step(const gr_step_desc* d, const gr_step_io* io, void* workspa
   P.tabw = ws_tab_words(d);
   P.pen_tab = (P.tabw > 0) ? reinterpret_cast<int*>(ws + o) : nullptr;
   const int rows = R * NB;
-  row_meta_kernel<<<(rows + 255) / 256, 256, 0, s>>>(P);
-  if (cudaGetLastError() != cudaSuccess) return GR_ERR_CUDA;
+  if (launch_pdl(row_meta_kernel, dim3((rows + 255) / 256), dim3(256), 0, s, P) != cudaSuccess) return GR_ERR_CUDA;
   return GR_OK;
 }
 

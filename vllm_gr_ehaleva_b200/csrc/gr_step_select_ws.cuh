@@ -188,6 +188,9 @@ __host__ __device__ __forceinline__ bool pen_used(const Params& P) {
 template <typename TL>
 __global__ void __launch_bounds__(256) pen_table_kernel(const __grid_constant__ Params P) {
   pdl_trigger();
+  // the histories and node ids may come from the previous step's merge, which
+  // the row records kernel waits for: wait for that grid before reading
+  pdl_wait();
   constexpr int ES = sizeof(TL);
   const int lane = lane_id();
   const int row = static_cast<int>(blockIdx.x) * (256 / 32) + warp_id();
@@ -248,9 +251,6 @@ __global__ void __launch_bounds__(256) pen_table_kernel(const __grid_constant__ 
     }
     for (int i = min(n_tab, P.tabw) + lane; i < P.tabw; i += 32) dst[i] = -1;
   }
-  // complete only after the row metadata kernel: the selecting kernel waits
-  // on this grid alone
-  pdl_wait();
 }
 
 // Producer warp: per row its record, its penalty table and flags, then its body.
