@@ -163,18 +163,18 @@ __device__ __forceinline__ uint32_t hash_find(const Slot* sl, uint32_t key) {
   return 0u;
 }
 
-// The streamers publish their lse bound after stages 0, 1, 3, 7, 15, 31 (a
-// row's stages 2^k - 1: the bound grows fastest early in the row, and every
+// The streamers publish their lse bound after stages 0, 2, 6, 14, 30 (a row's
+// stages 2^k - 2: the bound grows fastest early in the row, and every
 // publication is the streaming warps' longest chain; publishing after every
-// second or fourth stage measured slower).
-__host__ __device__ constexpr bool published(int ch) { return ch < 2 || ((ch + 1) & ch) == 0; }
-// The last published stage at or before stage ch (rows have at most kMaxRowStages <= 63 stages).
+// second or fourth stage, or after 0, 1, 3, 7, 15, measured slower).
+__host__ __device__ constexpr bool published(int ch) { return ((ch + 2) & (ch + 1)) == 0; }
+// The last published stage at or before stage ch (rows have at most kMaxRowStages <= 62 stages).
 __host__ __device__ constexpr int last_published(int ch) {
-  return ch < 2 ? ch : (ch >= 31 ? 31 : ch >= 15 ? 15 : ch >= 7 ? 7 : ch >= 3 ? 3 : 1);
+  return ch >= 30 ? 30 : ch >= 14 ? 14 : ch >= 6 ? 6 : ch >= 2 ? 2 : 0;
 }
-static_assert(kMaxRowStages <= 63, "last_published covers every stage index");
-static_assert(last_published(2) == 1 && last_published(5) == 3 && last_published(7) == 7 &&
-              last_published(30) == 15 && published(last_published(47)), "publication");
+static_assert(kMaxRowStages <= 62, "last_published covers every stage index");
+static_assert(published(0) && !published(1) && last_published(1) == 0 && last_published(5) == 2 &&
+              last_published(13) == 6 && last_published(29) == 14 && published(last_published(47)), "publication");
 
 // The published lower bound of a slot's row lse (-inf when none).
 __device__ __forceinline__ float lse_bound_of(const Slot* sl) {
@@ -445,8 +445,8 @@ __device__ __forceinline__ float sel_lse_bound(const sel::Slot* sl) {
 // Streamers: (max, sum exp) of every row, penalised columns left out; after
 // each stage the warp's log-sum-exp so far goes to the slot, and the stage's
 // last warp combines the sixteen into lse_ord before counting the stage done.
-// Only the stages the selectors read a bound after are published (0, 1, 3, 7,
-// 15, 31): the publication is the streamers' longest chain.
+// Only the stages the selectors read a bound after are published (0, 2, 6, 14,
+// 30): the publication is the streamers' longest chain.
 template <typename TL>
 __device__ void sel_stream_rows(const Params& P) {
   const Smem S = smem_view(P);
@@ -548,7 +548,7 @@ __device__ void sel_stream_rows(const Params& P) {
           if (sid + j * sel::kStrThreads < nvec) FastSum<TL>::add(vv[j], A2, C2, sacc0, sacc1);
       }
       // publish the warp's log-sum-exp so far at the stages the selectors read
-      // (stages 0, 1, 3, 7, 15, 31), then count the stage as published
+      // (stages 0, 2, 6, 14, 30), then count the stage as published
       if (sel::published(ch)) {
         float q0, q1, q2, q3;
         unpack2(sacc0, q0, q1);
