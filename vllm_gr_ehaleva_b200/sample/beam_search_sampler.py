@@ -61,8 +61,14 @@ def _per_request(v, R: int, device) -> Optional[torch.Tensor]:
     if isinstance(v, torch.Tensor):
         t = v.to(device=device, dtype=torch.float32).reshape(-1)
     else:
-        t = torch.tensor([float(x) for x in (v if isinstance(v, Sequence) else [v] * R)],
-                         dtype=torch.float32, device=device)
+        # host values go through pinned memory with an asynchronous copy: a
+        # copy from pageable memory would make the host wait for the stream
+        # (every step queued before this one) on every call
+        t = torch.tensor([float(x) for x in (v if isinstance(v, Sequence) else [v] * R)], dtype=torch.float32)
+        if torch.device(device).type == "cuda":
+            t = t.pin_memory().to(device=device, non_blocking=True)
+        else:
+            t = t.to(device=device)
     if t.numel() == 1 and R > 1:
         t = t.expand(R).contiguous()
     if t.numel() != R:
